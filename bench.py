@@ -1,0 +1,396 @@
+"""Benchmark of the paged-decode attention path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg5]
+
+Metric: paged-decode attention HBM GB/s (fraction of the
+measured HBM peak) and decode tok/s, at 1/2/4/8 B200.
+
+Workload (default cfg2 = configuration 2): the attention of a TinyLlama-1.1B
+decode step — 22 layers, 32 q / 4 kv heads, head_dim 64, bf16 — for 256
+requests per GPU with contexts ~ U[1024, 4096], page size 16, KV pre-filled
+N(0,1), page ids a random permutation of the pool. One step = the device
+plan + batch indices/positions once, then for each of the 22 layers the KV
+append of the step's token and the decode attention. Requests are sharded
+round-robin over GPUs (weak scaling: 256 per GPU), each GPU owning its pool;
+no data-path collective (gloo is used only for the barrier and the max over
+ranks of the timed region).
+
+value = algorithmic bytes of all ranks (every K/V element read once, q read,
+o written, appended rows read + written) / max-over-ranks device time.
+e2e = the same bytes / device time of the same step driven through the
+public API from pinned host buffers (tables, q, new K/V copied in; outputs
+copied out every layer).
+
+--impl reference: the reference's attention math on the host cores (the
+CPU oracle: fp32 eager attention over gathered pages), rank 0 only, each
+step a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+PKG = "llm-inference-runtime_b200"
+METRIC = "paged-decode attn HBM GB/s (% peak); decode tok/s at 1/2/4/8 B200"
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": smax, "reasons": ["no samples"]}
+        load = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+def _workload(args):
+    wl = importlib.import_module(PKG + ".workloads")
+    if args.workload == "cfg5":
+        return wl, wl.LLAMA3_8B, 512, 8192, 32768, 1, "cfg5 long-context split-KV decode"
+    return wl, wl.TINYLLAMA, 256, 1024, 4096, 22, "cfg2 TinyLlama-1.1B decode step attention"
+
+
+def _global_lengths(batch_total: int, lo: int, hi: int, seed: int = 0) -> np.ndarray:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(lo, hi + 1, (batch_total,), generator=g).numpy().astype(np.int64) + 1
+
+
+# ------------------------------------------------------------------ ours
+def run_ours(args):
+    rank, world, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lir = importlib.import_module(PKG)
+    lir.build.build()
+    fi = importlib.import_module(PKG + ".flashinfer_api")
+    wl, geom, per_gpu, lo, hi, layers, wname = _workload(args)
+    P = geom.page_size
+
+    # weak scaling: global batch per_gpu * world, request i on GPU i mod world
+    lengths_all = _global_lengths(per_gpu * world, lo, hi)
+    mine = wl.round_robin(per_gpu * world, world, rank)
+    prob = wl.make_decode_problem(geom, len(mine), 0, 0, seed=1000 + rank, device=dev,
+                                  num_layers=layers, lengths=lengths_all[mine])
+    B = prob.batch
+    indptr, indices, last = prob.device_tables(dev)
+    seq = torch.from_numpy(prob.lengths.astype(np.int32)).to(dev)
+    append_indptr = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    ws = torch.empty(128 << 20, dtype=torch.uint8, device=dev)
+    wrap = fi.BatchDecodeWithPagedKVCacheWrapper(ws, "HND")
+    q = prob.q
+    k_new, v_new = prob.k_new, prob.v_new
+    out = torch.empty_like(q)
+    pool = prob.pool
+
+    bytes_decode = prob.decode_bytes_per_layer()
+    bytes_append = prob.append_bytes_per_layer()
+    bytes_step = layers * (bytes_decode + bytes_append)
+    launches_per_step = 2 + 2 * layers  # positions + plan, then append + decode per layer
+
+    stream = torch.cuda.current_stream()
+    dec_events = []
+
+    def step(record: bool):
+        bi, pos = fi.get_batch_indices_positions(append_indptr, seq, B)
+        wrap.plan(indptr, indices, last, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim,
+                  P, q_data_type=q.dtype)
+        for layer in range(layers):
+            fi.append_paged_kv_cache(k_new, v_new, bi, pos, pool[layer], indices, indptr, last,
+                                     kv_layout="HND")
+            if record:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            wrap.run(q, pool[layer], out=out)
+            if record:
+                e1.record(stream)
+                dec_events.append((e0, e1))
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    lir._lib.check_device("bench warm-up")
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop()
+    ms_local = t0.elapsed_time(t1)
+    ms = _max_over_ranks(ms_local, world)
+    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in dec_events)
+    total_bytes = _sum_over_ranks(float(bytes_step) * args.steps, world)
+    value = total_bytes / (ms * 1e-3) / 1e9
+    tok_s = _sum_over_ranks(float(B) * args.steps, world) / (ms * 1e-3)
+    lir._lib.check_device("bench timed region")
+
+    # ---- end to end through the public API from pinned host memory
+    h_indptr = torch.from_numpy(prob.kv_indptr).pin_memory()
+    h_indices = torch.from_numpy(prob.kv_indices).pin_memory()
+    h_last = torch.from_numpy(prob.kv_last_page_len).pin_memory()
+    h_seq = seq.cpu().pin_memory()
+    h_q = q.cpu().pin_memory()
+    h_k = k_new.cpu().pin_memory()
+    h_v = v_new.cpu().pin_memory()
+    h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    d_q, d_k, d_v = torch.empty_like(q), torch.empty_like(k_new), torch.empty_like(v_new)
+    d_indptr, d_indices, d_last = (torch.empty_like(indptr), torch.empty_like(indices),
+                                   torch.empty_like(last))
+    d_seq = torch.empty_like(seq)
+    h2d = (h_indptr.numel() + h_indices.numel() + h_last.numel() + h_seq.numel()) * 4 + \
+        layers * (h_q.numel() + h_k.numel() + h_v.numel()) * 2
+    d2h = layers * h_out.numel() * 2
+
+    def e2e_step():
+        d_indptr.copy_(h_indptr, non_blocking=True)
+        d_indices.copy_(h_indices, non_blocking=True)
+        d_last.copy_(h_last, non_blocking=True)
+        d_seq.copy_(h_seq, non_blocking=True)
+        bi, pos = fi.get_batch_indices_positions(append_indptr, d_seq, B)
+        wrap.plan(d_indptr, d_indices, d_last, geom.num_qo_heads, geom.num_kv_heads,
+                  geom.head_dim, P, q_data_type=q.dtype)
+        for layer in range(layers):
+            d_q.copy_(h_q, non_blocking=True)
+            d_k.copy_(h_k, non_blocking=True)
+            d_v.copy_(h_v, non_blocking=True)
+            fi.append_paged_kv_cache(d_k, d_v, bi, pos, pool[layer], d_indices, d_indptr,
+                                     d_last, kv_layout="HND")
+            wrap.run(d_q, pool[layer], out=out)
+            h_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_ms = _max_over_ranks(t0.elapsed_time(t1), world)
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+
+    peak, peak_kind = _peaks()
+    achieved = bytes_decode / (dec_ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(prob_lengths=prob.lengths, geom=geom, layers=layers)
+    _barrier(world)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) q/K/V, random page permutation, random-init",
+            "config": {"workload": wname, "layers": layers,
+                       "num_qo_heads": geom.num_qo_heads, "num_kv_heads": geom.num_kv_heads,
+                       "head_dim": geom.head_dim, "page_size": P,
+                       "requests_per_gpu": B, "global_batch": per_gpu * world,
+                       "context": f"U[{lo},{hi}] + 1 appended",
+                       "parallelism": f"request-sharded x{world}, no collective",
+                       "l2": "inputs larger than L2 (KV of one layer "
+                             f"{bytes_decode / 1e6:.0f} MB vs 126 MB L2)"},
+            "decode_tok_s": round(tok_s, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": peak_kind, "kernel": "decode_kernel",
+                         "bytes_per_launch": bytes_decode,
+                         "avg_launch_ms": round(dec_ms, 5),
+                         "traffic": _traffic_from_profile(bytes_decode)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _traffic_from_profile(bytes_decode: int):
+    """DRAM bytes per decode launch from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", "decode_kernel_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    # captured on a smaller case; traffic scales with the KV bytes processed
+    return int(d["dram_bytes_per_launch"] * bytes_decode / d["algorithmic_bytes_per_launch"])
+
+
+# ------------------------------------------------------------- CPU side
+def cpu_baseline(prob_lengths: np.ndarray, geom, layers: int, budget_s: float = 15.0,
+                 sample: int = 16) -> dict:
+    """Times the CPU oracle (fp32 eager attention over gathered pages) on a
+    seeded sample of the workload's requests, one layer; reports GB/s of the
+    same algorithmic bytes."""
+    from oracle import cpu_baseline as cb
+    return cb.time_decode_sample(prob_lengths, geom, budget_s=budget_s, sample=sample)
+
+
+def run_reference(args):
+    rank, world, local = _dist()
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    wl, geom, per_gpu, lo, hi, layers, wname = _workload(args)
+    from oracle import cpu_baseline as cb
+    lengths_all = _global_lengths(per_gpu * world, lo, hi)
+    mine = wl.round_robin(per_gpu * world, world, 0)
+    res = cb.run_reference_arm(lengths_all[mine], geom, steps=args.steps, warmup=args.warmup)
+    line = {
+        "metric": METRIC, "value": round(res["value"], 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) q/K/V, random page permutation",
+        "config": {"workload": wname, "layers": layers, "num_qo_heads": geom.num_qo_heads,
+                   "num_kv_heads": geom.num_kv_heads, "head_dim": geom.head_dim,
+                   "page_size": geom.page_size, "requests_per_gpu": per_gpu,
+                   "global_batch": per_gpu * world, "context": f"U[{lo},{hi}] + 1 appended",
+                   "parallelism": "host cores of rank 0"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(res["value"], 3), "unit": "GB/s", "cores": res["cores"],
+                         "kind": "port", "sample": res["sample"]},
+        "e2e": {"value": round(res["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,176 @@
+/*
+ * paged_attn.h — C ABI of the B200 (sm_100a) paged-attention backend.
+ *
+ * These entry points replace the FlashInfer 0.6.11 calls that
+ * harsh-vsingh/LLM-Inference-Runtime makes from its monkey-patched LLaMA
+ * attention (src/models/llama.py) and its step executor
+ * (src/engine/runtime/step_executor.py). Each declaration names the
+ * reference call it stands in for.
+ *
+ * Conventions shared by every function:
+ *   - Plain pointers and sizes only. Device pointers are CUDA device
+ *     addresses; `stream` is a cudaStream_t passed as void* (NULL = legacy
+ *     default stream). Work is enqueued on `stream`; no call synchronises
+ *     the device except pa_device_status().
+ *   - The return value is a pa_status code (0 = success). Argument errors
+ *     are detected on the host before anything is launched. Errors that only
+ *     the device can see (page ids out of range, malformed indptr, bounded
+ *     waits that expired) are recorded in a per-device status word that
+ *     pa_device_status() reads and clears.
+ *   - KV pool layout is FlashInfer's: a page holds `page_size` tokens; the
+ *     key and value caches are addressed by base pointer plus element
+ *     strides (page, head, token), the last dimension (head_dim) contiguous.
+ *     For the engine's single 5-D pool [num_pages, 2, H_kv, P, D] ("HND")
+ *     the value base is key base + H_kv*P*D and page stride 2*H_kv*P*D.
+ *   - dtype codes: PA_DTYPE_F16 or PA_DTYPE_BF16 for q / k / v / pool / out.
+ *   - LSE values (optional outputs, merge inputs) are base-2:
+ *     log2(sum_j 2^(s_j)), s_j = sm_scale * log2(e) * <q, k_j>, which is
+ *     FlashInfer's convention.
+ */
+#ifndef PAGED_ATTN_H_
+#define PAGED_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum pa_status {
+  PA_OK = 0,
+  PA_ERR_INVALID_ARGUMENT = 1,   /* bad pointer, size, stride or alignment */
+  PA_ERR_UNSUPPORTED = 2,        /* head_dim / page_size / group size / dtype not built */
+  PA_ERR_WORKSPACE_TOO_SMALL = 3,
+  PA_ERR_CUDA = 4,               /* a CUDA runtime call or launch failed */
+  PA_ERR_DEVICE_CHECK = 5,       /* device-side validation failed (indptr, page id, last_page_len, position) */
+  PA_ERR_TIMEOUT = 6,            /* a bounded device-side wait expired */
+  PA_ERR_NOT_PLANNED = 7         /* run called on a workspace without a matching plan */
+};
+
+enum pa_dtype { PA_DTYPE_F16 = 0, PA_DTYPE_BF16 = 1 };
+
+enum pa_kv_layout { PA_LAYOUT_NHD = 0, PA_LAYOUT_HND = 1 };
+
+/* Describes one layer of the paged KV cache. */
+typedef struct pa_kv_cache {
+  const void* k_base;     /* device address of key page 0 */
+  const void* v_base;     /* device address of value page 0 */
+  int64_t page_stride;    /* elements between consecutive pages */
+  int64_t head_stride;    /* elements between consecutive kv heads inside a page */
+  int64_t token_stride;   /* elements between consecutive tokens inside a page */
+  int64_t num_pages;      /* pages addressable from k_base / v_base */
+  int32_t num_kv_heads;
+  int32_t page_size;
+  int32_t head_dim;
+  int32_t dtype;          /* enum pa_dtype */
+} pa_kv_cache;
+
+/* Human-readable name of a status code (static string). */
+const char* pa_status_string(int status);
+
+/* ABI version of this library (major * 100 + minor). */
+int pa_abi_version(void);
+
+/* Reads and clears the device-side status word of the current device.
+ * Synchronises the device. Returns PA_OK, PA_ERR_DEVICE_CHECK or
+ * PA_ERR_TIMEOUT (the first error recorded since the last read). */
+int pa_device_status(void);
+
+/* Replaces flashinfer.get_batch_indices_positions (called from
+ * src/models/llama.py:70-83, which step_executor.py:155 drives):
+ *   batch_indices[t] = b and positions[t] = seq_lens[b] - (append_indptr[b+1]
+ *   - append_indptr[b]) + (t - append_indptr[b]) for append_indptr[b] <= t <
+ *   append_indptr[b+1]. Entries t >= append_indptr[batch_size] (up to nnz)
+ *   get batch index -1 and position 0. */
+int pa_batch_indices_positions(const int32_t* append_indptr, const int32_t* seq_lens,
+                               int32_t batch_size, int32_t nnz, int32_t* batch_indices,
+                               int32_t* positions, void* stream);
+
+/* Replaces flashinfer.append_paged_kv_cache(..., kv_layout) (called at
+ * src/models/llama.py:188-210). Scatters append_key/append_value rows
+ * [nnz, H_kv, D] (strides in elements, last dim contiguous) into the pool:
+ *   page = kv_indices[kv_indptr[b] + pos / P], slot = pos % P,
+ *   with b = batch_indices[t], pos = positions[t].
+ * Rows whose page falls outside the request's pages or the pool are skipped
+ * and reported as PA_ERR_DEVICE_CHECK. Bit-exact copy. */
+int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
+                             const void* append_value, int64_t value_stride_n,
+                             int64_t value_stride_h, const int32_t* batch_indices,
+                             const int32_t* positions, int32_t nnz, const pa_kv_cache* cache,
+                             const int32_t* kv_indices, const int32_t* kv_indptr,
+                             int32_t batch_size, void* stream);
+
+/* Replaces flashinfer.apply_rope_pos_ids_inplace(q, k, pos_ids,
+ * rotary_dim, interleave, rope_scale, rope_theta) (src/models/llama.py:175-182).
+ * Rotates the first rotary_dim dims of every q row [nnz, H_q, D] and k row
+ * [nnz, H_kv, D] in place, angle = pos / rope_scale * rope_theta^(-2i/rotary_dim). */
+int pa_apply_rope_pos_ids_inplace(void* q, int64_t q_stride_n, int64_t q_stride_h, void* k,
+                                  int64_t k_stride_n, int64_t k_stride_h, const int32_t* pos_ids,
+                                  int32_t nnz, int32_t num_qo_heads, int32_t num_kv_heads,
+                                  int32_t head_dim, int32_t rotary_dim, int32_t interleave,
+                                  float rope_scale, float rope_theta, int32_t dtype, void* stream);
+
+/* Workspace bytes pa_decode_plan needs for this batch geometry. */
+size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
+                                 int32_t head_dim);
+
+/* Replaces BatchDecodeWithPagedKVCacheWrapper.plan / begin_forward
+ * (src/models/llama.py:119-147, called from step_executor.py:227-234).
+ * Runs on the device: validates the CSR table, splits the (request,
+ * kv-head, page) stream evenly over the persistent decode warps and writes
+ * that partition into `workspace`. Reused by every layer until the next plan. */
+int pa_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int32_t batch_size,
+                   int64_t num_kv_indices, int32_t num_qo_heads, int32_t num_kv_heads,
+                   int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* Replaces BatchDecodeWithPagedKVCacheWrapper.forward / run
+ * (src/models/llama.py:230-245). q [B, H_q, D] with strides in elements;
+ * out [B, H_q, D] contiguous; lse [B, H_q] float (may be NULL).
+ * sm_scale <= 0 selects 1/sqrt(head_dim). Split requests are merged by
+ * log-sum-exp inside the same launch. */
+int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                  const int32_t* kv_indices, const int32_t* kv_indptr,
+                  const int32_t* kv_last_page_len, int32_t batch_size, int32_t num_qo_heads,
+                  float sm_scale, void* workspace, size_t workspace_bytes, void* out, float* lse,
+                  void* stream);
+
+/* Workspace bytes pa_prefill_plan needs. */
+size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int32_t num_qo_heads,
+                                  int32_t num_kv_heads, int32_t head_dim);
+
+/* Replaces BatchPrefillWithPagedKVCacheWrapper.plan / begin_forward
+ * (src/models/llama.py:86-116, called from step_executor.py:157-165).
+ * Device-side: validates qo_indptr / kv_indptr / kv_last_page_len and writes
+ * the list of (request, kv-head, 128-row query tile) work items. */
+int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                    const int32_t* kv_last_page_len, int32_t batch_size, int64_t total_qo,
+                    int64_t num_kv_indices, int32_t num_qo_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Replaces BatchPrefillWithPagedKVCacheWrapper.forward(q, cache, causal)
+ * (src/models/llama.py:212-228). q [total_qo, H_q, D] (strides in elements),
+ * out [total_qo, H_q, D] contiguous, lse [total_qo, H_q] (may be NULL).
+ * causal != 0 aligns the mask bottom-right: query i of a request with
+ * qo_len rows and kv_len keys sees key j iff j <= i + kv_len - qo_len. */
+int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                   const int32_t* qo_indptr, const int32_t* kv_indices, const int32_t* kv_indptr,
+                   const int32_t* kv_last_page_len, int32_t batch_size, int64_t total_qo,
+                   int32_t num_qo_heads, int32_t causal, float sm_scale, void* workspace,
+                   size_t workspace_bytes, void* out, float* lse, void* stream);
+
+/* Replaces flashinfer.merge_states (the split-KV log-sum-exp merge):
+ * v [seq_len, num_states, num_heads, D] (dtype), s [seq_len, num_states,
+ * num_heads] float base-2 LSE -> v_merged [seq_len, num_heads, D] (dtype),
+ * s_merged [seq_len, num_heads] (may be NULL). */
+int pa_merge_states(const void* v, const float* s, int32_t seq_len, int32_t num_states,
+                    int32_t num_heads, int32_t head_dim, int32_t dtype, void* v_merged,
+                    float* s_merged, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGED_ATTN_H_ */

@@ -1,0 +1,402 @@
+// C ABI of the paged-attention backend (declarations: include/paged_attn.h).
+// Host-side argument checks, TMA descriptor encoding, launch configuration.
+// Single translation unit: every kernel header is included here so device
+// globals (the status word) need no relocatable device code.
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "decode.cuh"
+#include "ops.cuh"
+#include "prefill.cuh"
+
+namespace {
+
+using namespace pa;
+
+constexpr int kMaxDevices = 64;
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+
+int sm_count(int dev) {
+  static std::atomic<int> cache[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return 0;
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+// cudaFuncSetAttribute is per device; remember which (kernel, device) pairs
+// already allow their dynamic shared memory size.
+template <typename K>
+cudaError_t allow_smem(K kernel, int bytes, std::atomic<uint64_t>* done_mask, int dev) {
+  const uint64_t bit = uint64_t(1) << (dev & 63);
+  if (done_mask->load(std::memory_order_relaxed) & bit) return cudaSuccess;
+  cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done_mask->fetch_or(bit);
+  return e;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// True when the cache keeps the heads of a token next to each other
+// ("NHD": token stride > head stride). The tensor map then orders its dims
+// (D, H_kv, P, pages) so strides increase; otherwise (D, P, H_kv, pages).
+bool heads_inner(const pa_kv_cache& c) { return c.token_stride > c.head_stride; }
+
+// 4-D map over one of the K / V caches, 128-byte swizzled boxes of 64
+// columns x box_rows tokens of one head of one page. Either dim order lands
+// the box in shared memory as box_rows rows of 128 bytes.
+int encode_kv_map(CUtensorMap* map, const void* base, const pa_kv_cache& c, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return PA_ERR_CUDA;
+  const bool hi = heads_inner(c);
+  const cuuint64_t P = static_cast<cuuint64_t>(c.page_size);
+  const cuuint64_t H = static_cast<cuuint64_t>(c.num_kv_heads);
+  const cuuint64_t ts = static_cast<cuuint64_t>(c.token_stride) * 2;
+  const cuuint64_t hs = static_cast<cuuint64_t>(c.head_stride) * 2;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(c.head_dim), hi ? H : P, hi ? P : H,
+                              static_cast<cuuint64_t>(c.num_pages)};
+  const cuuint64_t strides[3] = {hi ? hs : ts, hi ? ts : hs,
+                                 static_cast<cuuint64_t>(c.page_stride) * 2};
+  const cuuint32_t br = static_cast<cuuint32_t>(box_rows);
+  const cuuint32_t box[4] = {64, hi ? 1u : br, hi ? br : 1u, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = c.dtype == PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PA_OK : PA_ERR_INVALID_ARGUMENT;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool valid_dtype(int dt) { return dt == PA_DTYPE_F16 || dt == PA_DTYPE_BF16; }
+
+// Checks a cache description for the attention kernels (TMA needs 16-byte
+// aligned bases and strides).
+int check_cache(const pa_kv_cache* c) {
+  if (c == nullptr || c->k_base == nullptr || c->v_base == nullptr) return PA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(c->dtype)) return PA_ERR_UNSUPPORTED;
+  if (c->num_kv_heads <= 0 || c->num_pages <= 0 || c->page_size <= 0 || c->head_dim <= 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(c->k_base) || !aligned16(c->v_base)) return PA_ERR_INVALID_ARGUMENT;
+  if (c->page_stride % 8 || c->head_stride % 8 || c->token_stride % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  return PA_OK;
+}
+
+int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? PA_OK : PA_ERR_CUDA;
+}
+
+int decode_warps_total(int dev) { return sm_count(dev) * kDecodeWarps; }
+
+template <typename T, int D>
+int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& prm, int dev,
+                  cudaStream_t stream) {
+  static std::atomic<uint64_t> done{0};
+  constexpr int smem = DecodeCfg<D>::kSmemBytes;
+  if (allow_smem(decode_kernel<T, D>, smem, &done, dev) != cudaSuccess) return PA_ERR_CUDA;
+  decode_kernel<T, D><<<sm_count(dev), kDecodeWarps * 32, smem, stream>>>(km, vm, prm);
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pa_status_string(int status) {
+  switch (status) {
+    case PA_OK: return "ok";
+    case PA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case PA_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case PA_ERR_CUDA: return "CUDA error";
+    case PA_ERR_DEVICE_CHECK: return "device-side validation failed";
+    case PA_ERR_TIMEOUT: return "bounded device wait expired";
+    case PA_ERR_NOT_PLANNED: return "run without a matching plan";
+    default: return "unknown status";
+  }
+}
+
+int pa_abi_version(void) { return 100; }
+
+int pa_device_status(void) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return PA_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_status, sizeof(int)) != cudaSuccess) return PA_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_status, &zero, sizeof(int)) != cudaSuccess) return PA_ERR_CUDA;
+  return v;
+}
+
+int pa_batch_indices_positions(const int32_t* append_indptr, const int32_t* seq_lens,
+                               int32_t batch_size, int32_t nnz, int32_t* batch_indices,
+                               int32_t* positions, void* stream) {
+  if (batch_size < 0 || nnz < 0) return PA_ERR_INVALID_ARGUMENT;
+  if (append_indptr == nullptr || (batch_size > 0 && seq_lens == nullptr)) return PA_ERR_INVALID_ARGUMENT;
+  if (nnz > 0 && (batch_indices == nullptr || positions == nullptr)) return PA_ERR_INVALID_ARGUMENT;
+  if (nnz == 0) return PA_OK;
+  batch_indices_positions_kernel<<<batch_size + 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      append_indptr, seq_lens, batch_size, nnz, batch_indices, positions);
+  return launch_status();
+}
+
+int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
+                             const void* append_value, int64_t value_stride_n,
+                             int64_t value_stride_h, const int32_t* batch_indices,
+                             const int32_t* positions, int32_t nnz, const pa_kv_cache* cache,
+                             const int32_t* kv_indices, const int32_t* kv_indptr,
+                             int32_t batch_size, void* stream) {
+  if (nnz < 0 || batch_size < 0) return PA_ERR_INVALID_ARGUMENT;
+  if (nnz == 0) return PA_OK;
+  if (cache == nullptr || append_key == nullptr || append_value == nullptr ||
+      batch_indices == nullptr || positions == nullptr || kv_indices == nullptr ||
+      kv_indptr == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(cache->dtype)) return PA_ERR_UNSUPPORTED;
+  if (cache->k_base == nullptr || cache->v_base == nullptr || cache->page_size <= 0 ||
+      cache->num_kv_heads <= 0 || cache->head_dim <= 0 || cache->head_dim % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  // 16-byte vector copies: rows and row starts must be 16-byte aligned.
+  if (!aligned16(append_key) || !aligned16(append_value) || !aligned16(cache->k_base) ||
+      !aligned16(cache->v_base))
+    return PA_ERR_INVALID_ARGUMENT;
+  if (key_stride_n % 8 || key_stride_h % 8 || value_stride_n % 8 || value_stride_h % 8 ||
+      cache->page_stride % 8 || cache->head_stride % 8 || cache->token_stride % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  AppendParams p;
+  p.key = static_cast<const uint8_t*>(append_key);
+  p.value = static_cast<const uint8_t*>(append_value);
+  p.key_stride_n = key_stride_n * 2;
+  p.key_stride_h = key_stride_h * 2;
+  p.value_stride_n = value_stride_n * 2;
+  p.value_stride_h = value_stride_h * 2;
+  p.batch_indices = batch_indices;
+  p.positions = positions;
+  p.nnz = nnz;
+  p.k_base = static_cast<uint8_t*>(const_cast<void*>(cache->k_base));
+  p.v_base = static_cast<uint8_t*>(const_cast<void*>(cache->v_base));
+  p.page_stride = cache->page_stride * 2;
+  p.head_stride = cache->head_stride * 2;
+  p.token_stride = cache->token_stride * 2;
+  p.num_pages = cache->num_pages;
+  p.kv_indices = kv_indices;
+  p.kv_indptr = kv_indptr;
+  p.batch = batch_size;
+  p.num_kv_heads = cache->num_kv_heads;
+  p.page_size = cache->page_size;
+  p.row_chunks = cache->head_dim * 2 / 16;
+  const int64_t work = static_cast<int64_t>(nnz) * cache->num_kv_heads * p.row_chunks * 2;
+  const int dev = current_device();
+  const int64_t max_blocks = static_cast<int64_t>(sm_count(dev) > 0 ? sm_count(dev) : 148) * 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
+  append_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
+int pa_apply_rope_pos_ids_inplace(void* q, int64_t q_stride_n, int64_t q_stride_h, void* k,
+                                  int64_t k_stride_n, int64_t k_stride_h, const int32_t* pos_ids,
+                                  int32_t nnz, int32_t num_qo_heads, int32_t num_kv_heads,
+                                  int32_t head_dim, int32_t rotary_dim, int32_t interleave,
+                                  float rope_scale, float rope_theta, int32_t dtype,
+                                  void* stream) {
+  if (nnz < 0 || num_qo_heads < 0 || num_kv_heads < 0) return PA_ERR_INVALID_ARGUMENT;
+  if (nnz == 0 || num_qo_heads + num_kv_heads == 0) return PA_OK;
+  if (pos_ids == nullptr || (num_qo_heads > 0 && q == nullptr) ||
+      (num_kv_heads > 0 && k == nullptr))
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(dtype)) return PA_ERR_UNSUPPORTED;
+  if (rotary_dim <= 0 || rotary_dim % 2 || rotary_dim > head_dim) return PA_ERR_INVALID_ARGUMENT;
+  if (!(rope_scale > 0.f) || !(rope_theta > 0.f)) return PA_ERR_INVALID_ARGUMENT;
+  const int64_t work = static_cast<int64_t>(nnz) * (num_qo_heads + num_kv_heads) * (rotary_dim / 2);
+  const int dev = current_device();
+  const int64_t max_blocks = static_cast<int64_t>(sm_count(dev) > 0 ? sm_count(dev) : 148) * 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
+  const float inv_scale = 1.0f / rope_scale;
+  const float log2_theta = std::log2(rope_theta);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == PA_DTYPE_BF16)
+    rope_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        static_cast<__nv_bfloat16*>(q), q_stride_n, q_stride_h, static_cast<__nv_bfloat16*>(k),
+        k_stride_n, k_stride_h, pos_ids, nnz, num_qo_heads, num_kv_heads, rotary_dim, interleave,
+        inv_scale, log2_theta);
+  else
+    rope_kernel<__half><<<blocks, 256, 0, st>>>(
+        static_cast<__half*>(q), q_stride_n, q_stride_h, static_cast<__half*>(k), k_stride_n,
+        k_stride_h, pos_ids, nnz, num_qo_heads, num_kv_heads, rotary_dim, interleave, inv_scale,
+        log2_theta);
+  return launch_status();
+}
+
+size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
+                                 int32_t head_dim) {
+  (void)num_qo_heads;
+  const int dev = current_device();
+  if (dev < 0 || batch_size < 0 || num_kv_heads <= 0 || head_dim <= 0) return 0;
+  return decode_ws_layout(decode_warps_total(dev), batch_size, num_kv_heads, head_dim).total;
+}
+
+int pa_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int32_t batch_size,
+                   int64_t num_kv_indices, int32_t num_qo_heads, int32_t num_kv_heads,
+                   int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (kv_indptr == nullptr || kv_last_page_len == nullptr || workspace == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size <= 0 || num_kv_indices < 0 || num_qo_heads <= 0 || num_kv_heads <= 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (num_qo_heads % num_kv_heads) return PA_ERR_INVALID_ARGUMENT;
+  if (num_qo_heads / num_kv_heads > kMaxGroup) return PA_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return PA_ERR_UNSUPPORTED;
+  if (page_size != kPage) return PA_ERR_UNSUPPORTED;
+  if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  const int W = decode_warps_total(dev);
+  if (W <= 0) return PA_ERR_CUDA;
+  const DecodeWsLayout L = decode_ws_layout(W, batch_size, num_kv_heads, head_dim);
+  if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  decode_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      kv_indptr, kv_last_page_len, batch_size, num_kv_heads, num_qo_heads, head_dim, page_size,
+      num_kv_indices, W, /*min_per_warp=*/8, static_cast<uint8_t*>(workspace));
+  return launch_status();
+}
+
+int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                  const int32_t* kv_indices, const int32_t* kv_indptr,
+                  const int32_t* kv_last_page_len, int32_t batch_size, int32_t num_qo_heads,
+                  float sm_scale, void* workspace, size_t workspace_bytes, void* out, float* lse,
+                  void* stream) {
+  int st = check_cache(cache);
+  if (st != PA_OK) return st;
+  if (q == nullptr || out == nullptr || kv_indices == nullptr || kv_indptr == nullptr ||
+      kv_last_page_len == nullptr || workspace == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size <= 0 || num_qo_heads <= 0) return PA_ERR_INVALID_ARGUMENT;
+  const int hkv = cache->num_kv_heads, D = cache->head_dim;
+  if (num_qo_heads % hkv) return PA_ERR_INVALID_ARGUMENT;
+  const int G = num_qo_heads / hkv;
+  if (G > kMaxGroup) return PA_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return PA_ERR_UNSUPPORTED;
+  if (cache->page_size != kPage) return PA_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(out) || q_stride_n % 8 || q_stride_h % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  const int W = decode_warps_total(dev);
+  if (W <= 0) return PA_ERR_CUDA;
+  const DecodeWsLayout L = decode_ws_layout(W, batch_size, hkv, D);
+  if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  CUtensorMap km, vm;
+  if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage)) != PA_OK) return st;
+  if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage)) != PA_OK) return st;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  DecodeParams p;
+  p.q = q;
+  p.q_stride_n = q_stride_n;
+  p.q_stride_h = q_stride_h;
+  p.out = out;
+  p.lse = lse;
+  p.kv_indices = kv_indices;
+  p.kv_indptr = kv_indptr;
+  p.kv_last_page_len = kv_last_page_len;
+  p.batch_size = batch_size;
+  p.num_qo_heads = num_qo_heads;
+  p.num_kv_heads = hkv;
+  p.group = G;
+  p.num_pages = cache->num_pages;
+  p.heads_inner = heads_inner(*cache) ? 1 : 0;
+  const float scale = sm_scale > 0.f ? sm_scale : 1.0f / std::sqrt(static_cast<float>(D));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.hdr = reinterpret_cast<const DecodePlanHeader*>(ws + L.hdr);
+  p.warp_start = reinterpret_cast<const int4*>(ws + L.warp_start);
+  p.empty = reinterpret_cast<const int32_t*>(ws + L.empty);
+  p.counter = reinterpret_cast<int32_t*>(ws + L.counter);
+  p.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
+  p.part_o = reinterpret_cast<float*>(ws + L.part_o);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cache->dtype == PA_DTYPE_BF16)
+    return D == 64 ? launch_decode<__nv_bfloat16, 64>(km, vm, p, dev, s)
+                   : launch_decode<__nv_bfloat16, 128>(km, vm, p, dev, s);
+  return D == 64 ? launch_decode<__half, 64>(km, vm, p, dev, s)
+                 : launch_decode<__half, 128>(km, vm, p, dev, s);
+}
+
+int pa_merge_states(const void* v, const float* s, int32_t seq_len, int32_t num_states,
+                    int32_t num_heads, int32_t head_dim, int32_t dtype, void* v_merged,
+                    float* s_merged, void* stream) {
+  if (seq_len < 0 || num_states <= 0 || num_heads <= 0 || head_dim <= 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (seq_len == 0) return PA_OK;
+  if (v == nullptr || s == nullptr || v_merged == nullptr) return PA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(dtype)) return PA_ERR_UNSUPPORTED;
+  const int64_t items = static_cast<int64_t>(seq_len) * num_heads;
+  const int blocks = static_cast<int>((items + 7) / 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == PA_DTYPE_BF16)
+    merge_states_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(v), s, seq_len, num_states, num_heads, head_dim,
+        static_cast<__nv_bfloat16*>(v_merged), s_merged);
+  else
+    merge_states_kernel<__half><<<blocks, 256, 0, st>>>(
+        static_cast<const __half*>(v), s, seq_len, num_states, num_heads, head_dim,
+        static_cast<__half*>(v_merged), s_merged);
+  return launch_status();
+}
+
+size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int32_t num_qo_heads,
+                                  int32_t num_kv_heads, int32_t head_dim) {
+  return prefill_workspace_bytes(batch_size, max_total_qo, num_qo_heads, num_kv_heads, head_dim);
+}
+
+int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                    const int32_t* kv_last_page_len, int32_t batch_size, int64_t total_qo,
+                    int64_t num_kv_indices, int32_t num_qo_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  return prefill_plan(qo_indptr, kv_indptr, kv_last_page_len, batch_size, total_qo,
+                      num_kv_indices, num_qo_heads, num_kv_heads, head_dim, page_size, workspace,
+                      workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                   const int32_t* qo_indptr, const int32_t* kv_indices, const int32_t* kv_indptr,
+                   const int32_t* kv_last_page_len, int32_t batch_size, int64_t total_qo,
+                   int32_t num_qo_heads, int32_t causal, float sm_scale, void* workspace,
+                   size_t workspace_bytes, void* out, float* lse, void* stream) {
+  int st = check_cache(cache);
+  if (st != PA_OK) return st;
+  return prefill_run(q, q_stride_n, q_stride_h, *cache, qo_indptr, kv_indices, kv_indptr,
+                     kv_last_page_len, batch_size, total_qo, num_qo_heads, causal, sm_scale,
+                     workspace, workspace_bytes, out, lse, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
