@@ -72,6 +72,19 @@ def test_decode_matches_transformers_eager_fixture(fi, case):
     _check(got, case["out"])
 
 
+@pytest.mark.parametrize("case", [c for c in load_attention_cases() if c["mode"] == "decode"],
+                         ids=lambda c: c["name"])
+def test_decode_matches_flashinfer_outputs(fi, case):
+    """Against FlashInfer 0.6.11's own B200 outputs on the same inputs
+    (tests/golden/flashinfer_outputs.npz)."""
+    import os
+    from conftest import GOLDEN
+    z = np.load(os.path.join(GOLDEN, "flashinfer_outputs.npz"))
+    got = _decode(fi, case["q"], case["pool"], case["kv_indptr"], case["kv_indices"],
+                  case["kv_last_page_len"], layout=case["layout"])
+    _check(got, torch.from_numpy(z[case["name"] + "__out"]))
+
+
 @pytest.mark.parametrize("geom_name,lengths", [
     ("TINYLLAMA", [1, 15, 16, 17, 31, 32, 33, 255, 256, 257]),
     ("LLAMA3_8B", [1, 16, 17, 100, 4000]),
@@ -204,8 +217,9 @@ def test_config4_radix_shared_prefix_decode(fi, workloads):
     np.cumsum([len(t) for t in tables_], out=indptr[1:])
     indices = np.array([b for t in tables_ for b in t], dtype=np.int32)
     last = np.array([L - (math.ceil(L / P) - 1) * P for L in lens], dtype=np.int32)
+    # q and a 2048-page pool; the tables come from the radix cache above
     prob = workloads.make_decode_problem(geom, 64, 0, 0, seed=12, num_layers=1,
-                                         lengths=np.array(lens), pool_pages=2048)
+                                         lengths=np.ones(64, dtype=np.int64), pool_pages=2048)
     got = _decode(fi, prob.q, prob.pool[0], indptr, indices, last)
     want, _ = attention.decode(prob.q, prob.pool[0].float(), indptr, indices, last)
     _check(got, want)

@@ -232,3 +232,31 @@ def test_lse_merge_identity():
                                    torch.stack([la, lb], 1).numpy())
     assert np.allclose(vm, o.numpy(), atol=1e-5)
     assert np.allclose(sm, l2.numpy(), atol=1e-5)
+
+
+def _flashinfer_outputs():
+    import os
+    from conftest import GOLDEN
+    path = os.path.join(GOLDEN, "flashinfer_outputs.npz")
+    return np.load(path) if os.path.exists(path) else None
+
+
+@pytest.mark.parametrize("case", load_attention_cases(), ids=lambda c: c["name"])
+def test_attention_oracle_matches_flashinfer_on_b200(case):
+    """The oracle against FlashInfer 0.6.11 itself (the reference's GPU path),
+    run on a B200 by tests/golden/make_flashinfer_golden.py. FlashInfer's
+    outputs are bf16, so the north-star bf16 tolerance applies."""
+    z = _flashinfer_outputs()
+    assert z is not None, "tests/golden/flashinfer_outputs.npz missing"
+    assert bytes(z["flashinfer_version"]).decode().startswith("0.6.11")
+    want = torch.from_numpy(z[case["name"] + "__out"])
+    pool = case["pool"].to(torch.float32)
+    if case["mode"] == "decode":
+        got, _ = attention.decode(case["q"], pool, case["kv_indptr"], case["kv_indices"],
+                                  case["kv_last_page_len"], layout=case["layout"])
+    else:
+        got, _ = attention.prefill(case["q"], case["qo_indptr"], pool, case["kv_indptr"],
+                                   case["kv_indices"], case["kv_last_page_len"], causal=True,
+                                   layout=case["layout"])
+    mx, mean, ok = attention.compare(want, got)
+    assert ok, f"max-abs {mx:.3e} mean-abs {mean:.3e}"
