@@ -169,6 +169,32 @@ int pa_merge_states(const void* v, const float* s, int32_t seq_len, int32_t num_
                     int32_t num_heads, int32_t head_dim, int32_t dtype, void* v_merged,
                     float* s_merged, void* stream);
 
+/* Size of the static device scratch that pa_decode_noalloc uses (24 MiB). */
+#define PA_NOALLOC_SCRATCH_BYTES (24u * 1024u * 1024u)
+
+/* No counterpart in the reference (FlashInfer always takes a caller-owned
+ * workspace). Decode attention — plan and run in one call — that allocates
+ * nothing and needs no workspace: for callers that cannot allocate device
+ * memory, such as C / FFI hosts that only hold buffers another runtime
+ * allocated (the pool, q, out) and have no allocator of their own, or
+ * serving loops that must not call cudaMalloc once the KV pool has claimed
+ * most of HBM (it can fail then, and it synchronises the device).
+ * Arguments mean what they mean for pa_decode_plan + pa_decode_run.
+ * Scratch (plan, split-KV partials, merge counters) lives in one static
+ * device array of PA_NOALLOC_SCRATCH_BYTES that every GPU loading this
+ * library holds until exit. Batches whose scratch would exceed it return
+ * PA_ERR_WORKSPACE_TOO_SMALL before anything is launched.
+ * The first call on a device looks up that array's device address (with
+ * that device current); make the first call before any stream capture.
+ * All calls share the one array and the plan is rewritten (and the merge
+ * counters cleared) by every call, so calls whose GPU work overlaps — two
+ * streams, or two host threads on the same device — race; serialise them. */
+int pa_decode_noalloc(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                      const pa_kv_cache* cache, const int32_t* kv_indices,
+                      const int32_t* kv_indptr, const int32_t* kv_last_page_len,
+                      int32_t batch_size, int64_t num_kv_indices, int32_t num_qo_heads,
+                      float sm_scale, void* out, float* lse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,8 @@ PA_ERR_NOT_PLANNED = 7
 PA_DTYPE_F16 = 0
 PA_DTYPE_BF16 = 1
 
+PA_NOALLOC_SCRATCH_BYTES = 24 * 1024 * 1024
+
 
 class PagedKVCache(ctypes.Structure):
     """Mirror of ``pa_kv_cache``."""
@@ -88,6 +90,11 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int64, POINTER(PagedKVCache), c_void_p, c_void_p, c_void_p,
          c_void_p, c_int32, c_int64, c_int32, c_int32, c_float, c_void_p, c_size_t, c_void_p,
          c_void_p, c_void_p],
+    ),
+    "pa_decode_noalloc": (
+        c_int32,
+        [c_void_p, c_int64, c_int64, POINTER(PagedKVCache), c_void_p, c_void_p, c_void_p, c_int32,
+         c_int64, c_int32, c_float, c_void_p, c_void_p, c_void_p],
     ),
     "pa_merge_states": (
         c_int32,

@@ -400,3 +400,52 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode: the same plan and run kernels with their scratch in
+// a static device array instead of a caller workspace.
+namespace {
+
+__device__ __align__(256) uint8_t g_noalloc_scratch[PA_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch for device `dev`, looked up once per
+// device with that device current. In host code the symbol itself is only a
+// host-side stand-in, never a device address.
+void* noalloc_scratch(int dev) {
+  static std::atomic<void*> addr[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  void* p = addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return nullptr;
+    addr[dev].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+}  // namespace
+
+extern "C" int pa_decode_noalloc(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                                 const pa_kv_cache* cache, const int32_t* kv_indices,
+                                 const int32_t* kv_indptr, const int32_t* kv_last_page_len,
+                                 int32_t batch_size, int64_t num_kv_indices, int32_t num_qo_heads,
+                                 float sm_scale, void* out, float* lse, void* stream) {
+  int st = check_cache(cache);
+  if (st != PA_OK) return st;
+  if (batch_size <= 0 || num_qo_heads <= 0) return PA_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  const int W = decode_warps_total(dev);
+  if (W <= 0) return PA_ERR_CUDA;
+  const size_t need =
+      decode_ws_layout(W, batch_size, cache->num_kv_heads, cache->head_dim).total;
+  if (need > PA_NOALLOC_SCRATCH_BYTES) return PA_ERR_WORKSPACE_TOO_SMALL;
+  void* scratch = noalloc_scratch(dev);
+  if (scratch == nullptr) return PA_ERR_CUDA;
+  st = pa_decode_plan(kv_indptr, kv_last_page_len, batch_size, num_kv_indices, num_qo_heads,
+                      cache->num_kv_heads, cache->head_dim, cache->page_size, scratch,
+                      PA_NOALLOC_SCRATCH_BYTES, stream);
+  if (st != PA_OK) return st;
+  return pa_decode_run(q, q_stride_n, q_stride_h, cache, kv_indices, kv_indptr, kv_last_page_len,
+                       batch_size, num_qo_heads, sm_scale, scratch, PA_NOALLOC_SCRATCH_BYTES, out,
+                       lse, stream);
+}
