@@ -72,9 +72,11 @@ EncodeTiledFn encode_fn() {
 bool heads_inner(const pa_kv_cache& c) { return c.token_stride > c.head_stride; }
 
 // 4-D map over one of the K / V caches, 128-byte swizzled boxes of 64
-// columns x box_rows tokens of one head of one page. Either dim order lands
-// the box in shared memory as box_rows rows of 128 bytes.
-int encode_kv_map(CUtensorMap* map, const void* base, const pa_kv_cache& c, int box_rows) {
+// columns x box_rows tokens x box_heads heads of one page. The box lands in
+// shared memory as box_rows * box_heads rows of 128 bytes, head-major for
+// HND pools and token-major for NHD pools.
+int encode_kv_map(CUtensorMap* map, const void* base, const pa_kv_cache& c, int box_rows,
+                  int box_heads) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return PA_ERR_CUDA;
   const bool hi = heads_inner(c);
@@ -87,7 +89,8 @@ int encode_kv_map(CUtensorMap* map, const void* base, const pa_kv_cache& c, int 
   const cuuint64_t strides[3] = {hi ? hs : ts, hi ? ts : hs,
                                  static_cast<cuuint64_t>(c.page_stride) * 2};
   const cuuint32_t br = static_cast<cuuint32_t>(box_rows);
-  const cuuint32_t box[4] = {64, hi ? 1u : br, hi ? br : 1u, 1};
+  const cuuint32_t bh = static_cast<cuuint32_t>(box_heads);
+  const cuuint32_t box[4] = {64, hi ? bh : br, hi ? br : bh, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt = c.dtype == PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -119,15 +122,38 @@ int launch_status() {
   return e == cudaSuccess ? PA_OK : PA_ERR_CUDA;
 }
 
-int decode_warps_total(int dev) { return sm_count(dev) * kDecodeWarps; }
+// Decode partition for a cache shape on device `dev`: one CTA per SM, each
+// holding DecodeGeom::groups_per_cta groups.
+struct DecodePlanShape {
+  DecodeGeom g;
+  int ctas;
+  int units;  // groups in the grid
+};
+
+bool decode_shape(int dev, int hkv, int head_dim, DecodePlanShape* s) {
+  if (!decode_geom(hkv, head_dim, &s->g)) return false;
+  s->ctas = sm_count(dev);
+  s->units = s->ctas * s->g.groups_per_cta;
+  return s->ctas > 0;
+}
+
+size_t decode_ws_bytes(const DecodePlanShape& s, int batch, int hkv, int head_dim) {
+  return decode_ws_layout(s.units, batch, hkv, head_dim, s.g.hb).total;
+}
 
 template <typename T, int D>
-int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& prm, int dev,
-                  cudaStream_t stream) {
-  static std::atomic<uint64_t> done{0};
-  constexpr int smem = DecodeCfg<D>::kSmemBytes;
-  if (allow_smem(decode_kernel<T, D>, smem, &done, dev) != cudaSuccess) return PA_ERR_CUDA;
-  decode_kernel<T, D><<<sm_count(dev), kDecodeWarps * 32, smem, stream>>>(km, vm, prm);
+int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& prm,
+                  const DecodePlanShape& sh, int dev, cudaStream_t stream) {
+  // Largest dynamic shared memory already allowed for this kernel, per device.
+  static std::atomic<int> allowed[kMaxDevices];
+  if (dev < 0 || dev >= kMaxDevices) return PA_ERR_CUDA;
+  if (allowed[dev].load(std::memory_order_relaxed) < sh.g.smem_bytes) {
+    if (cudaFuncSetAttribute(decode_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             sh.g.smem_bytes) != cudaSuccess)
+      return PA_ERR_CUDA;
+    allowed[dev].store(sh.g.smem_bytes, std::memory_order_relaxed);
+  }
+  decode_kernel<T, D><<<sh.ctas, sh.g.threads, sh.g.smem_bytes, stream>>>(km, vm, prm);
   return launch_status();
 }
 
@@ -264,7 +290,9 @@ size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32
   (void)num_qo_heads;
   const int dev = current_device();
   if (dev < 0 || batch_size < 0 || num_kv_heads <= 0 || head_dim <= 0) return 0;
-  return decode_ws_layout(decode_warps_total(dev), batch_size, num_kv_heads, head_dim).total;
+  DecodePlanShape sh;
+  if (!decode_shape(dev, num_kv_heads, head_dim, &sh)) return 0;
+  return decode_ws_bytes(sh, batch_size, num_kv_heads, head_dim);
 }
 
 int pa_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int32_t batch_size,
@@ -281,13 +309,14 @@ int pa_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, in
   if (page_size != kPage) return PA_ERR_UNSUPPORTED;
   if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
   const int dev = current_device();
-  const int W = decode_warps_total(dev);
-  if (W <= 0) return PA_ERR_CUDA;
-  const DecodeWsLayout L = decode_ws_layout(W, batch_size, num_kv_heads, head_dim);
-  if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  DecodePlanShape sh;
+  if (!decode_shape(dev, num_kv_heads, head_dim, &sh))
+    return dev < 0 ? PA_ERR_CUDA : PA_ERR_UNSUPPORTED;
+  if (decode_ws_bytes(sh, batch_size, num_kv_heads, head_dim) > workspace_bytes)
+    return PA_ERR_WORKSPACE_TOO_SMALL;
   decode_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
       kv_indptr, kv_last_page_len, batch_size, num_kv_heads, num_qo_heads, head_dim, page_size,
-      num_kv_indices, W, /*min_per_warp=*/8, static_cast<uint8_t*>(workspace));
+      num_kv_indices, sh.units, sh.g.hb, /*min_per_group=*/4, static_cast<uint8_t*>(workspace));
   return launch_status();
 }
 
@@ -311,13 +340,13 @@ int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const p
   if (!aligned16(q) || !aligned16(out) || q_stride_n % 8 || q_stride_h % 8)
     return PA_ERR_INVALID_ARGUMENT;
   const int dev = current_device();
-  const int W = decode_warps_total(dev);
-  if (W <= 0) return PA_ERR_CUDA;
-  const DecodeWsLayout L = decode_ws_layout(W, batch_size, hkv, D);
+  DecodePlanShape sh;
+  if (!decode_shape(dev, hkv, D, &sh)) return dev < 0 ? PA_ERR_CUDA : PA_ERR_UNSUPPORTED;
+  const DecodeWsLayout L = decode_ws_layout(sh.units, batch_size, hkv, D, sh.g.hb);
   if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
   CUtensorMap km, vm;
-  if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage)) != PA_OK) return st;
-  if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage)) != PA_OK) return st;
+  if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage, sh.g.hb)) != PA_OK) return st;
+  if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage, sh.g.hb)) != PA_OK) return st;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   DecodeParams p;
   p.q = q;
@@ -337,17 +366,22 @@ int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const p
   const float scale = sm_scale > 0.f ? sm_scale : 1.0f / std::sqrt(static_cast<float>(D));
   p.scale_log2 = scale * 1.4426950408889634f;
   p.hdr = reinterpret_cast<const DecodePlanHeader*>(ws + L.hdr);
-  p.warp_start = reinterpret_cast<const int4*>(ws + L.warp_start);
+  p.unit_start = reinterpret_cast<const int4*>(ws + L.unit_start);
+  p.hb = sh.g.hb;
+  p.nhb = sh.g.nhb;
+  p.groups_per_cta = sh.g.groups_per_cta;
+  p.stages = sh.g.stages;
+  p.stage_bytes = sh.g.stage_bytes;
   p.empty = reinterpret_cast<const int32_t*>(ws + L.empty);
   p.counter = reinterpret_cast<int32_t*>(ws + L.counter);
   p.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
   p.part_o = reinterpret_cast<float*>(ws + L.part_o);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cache->dtype == PA_DTYPE_BF16)
-    return D == 64 ? launch_decode<__nv_bfloat16, 64>(km, vm, p, dev, s)
-                   : launch_decode<__nv_bfloat16, 128>(km, vm, p, dev, s);
-  return D == 64 ? launch_decode<__half, 64>(km, vm, p, dev, s)
-                 : launch_decode<__half, 128>(km, vm, p, dev, s);
+    return D == 64 ? launch_decode<__nv_bfloat16, 64>(km, vm, p, sh, dev, s)
+                   : launch_decode<__nv_bfloat16, 128>(km, vm, p, sh, dev, s);
+  return D == 64 ? launch_decode<__half, 64>(km, vm, p, sh, dev, s)
+                 : launch_decode<__half, 128>(km, vm, p, sh, dev, s);
 }
 
 int pa_merge_states(const void* v, const float* s, int32_t seq_len, int32_t num_states,
@@ -434,10 +468,10 @@ extern "C" int pa_decode_noalloc(const void* q, int64_t q_stride_n, int64_t q_st
   if (st != PA_OK) return st;
   if (batch_size <= 0 || num_qo_heads <= 0) return PA_ERR_INVALID_ARGUMENT;
   const int dev = current_device();
-  const int W = decode_warps_total(dev);
-  if (W <= 0) return PA_ERR_CUDA;
-  const size_t need =
-      decode_ws_layout(W, batch_size, cache->num_kv_heads, cache->head_dim).total;
+  DecodePlanShape sh;
+  if (!decode_shape(dev, cache->num_kv_heads, cache->head_dim, &sh))
+    return dev < 0 ? PA_ERR_CUDA : PA_ERR_UNSUPPORTED;
+  const size_t need = decode_ws_bytes(sh, batch_size, cache->num_kv_heads, cache->head_dim);
   if (need > PA_NOALLOC_SCRATCH_BYTES) return PA_ERR_WORKSPACE_TOO_SMALL;
   void* scratch = noalloc_scratch(dev);
   if (scratch == nullptr) return PA_ERR_CUDA;

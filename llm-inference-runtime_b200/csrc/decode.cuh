@@ -5,51 +5,101 @@
 // o[b, hq] = softmax(sm_scale * q[b, hq] . K_b,hkv^T) V_b,hkv over the
 // request's kv_len = (pages - 1) * P + kv_last_page_len[b] keys, hkv = hq / g.
 //
-// Design (HBM-bound; one page of one kv head = P x D contiguous elements):
-//   * The work stream is every (request b, kv head h, page j) in that order.
-//     decode_plan_kernel cuts it into equal runs of Q page-heads, one run per
-//     persistent warp, so every warp moves the same number of bytes however
-//     skewed the context lengths are (split-KV without a host-side plan).
-//   * Each warp owns a ring of shared-memory stages. Lane 0 fills a stage with
-//     two tiled TMA loads (K tile and V tile of one page-head, 128-byte
-//     swizzle) completing on the stage's mbarrier, and keeps the ring full
-//     ahead of the warp's own compute. Warps never wait on each other.
+// Design (HBM-bound). A page of the engine's pool holds K then V of every kv
+// head contiguously (16 KiB for 4 heads x 64 dims, 64 KiB for 8 x 128), and
+// random whole-page reads stream ~15 % faster from HBM3e than the 2 KiB
+// per-head pieces a head-at-a-time kernel would issue. So:
+//   * A "group" is one warp per kv head of a head block (HB = min(H_kv, 8)
+//     heads). The group walks a run of pages; each stage of its shared-memory
+//     ring holds one page of the head block — K and V, every panel — fetched
+//     by one tiled TMA load per (K|V, 64-column panel) that completes on the
+//     stage's mbarrier. Warp h of the group reads head h's rows.
+//   * The work stream is every (request b, head block, page j) in that order.
+//     decode_plan_kernel cuts it into equal runs of Q pages, one per group, so
+//     every group moves the same bytes however skewed the context lengths are
+//     (split-KV with no host-side plan).
+//   * A stage is refilled by whichever warp of the group releases it last
+//     (shared-memory arrival counter), with a page id loaded one refill ahead.
+//     No warp ever blocks on another warp's progress.
 //   * The g query heads of a kv head are the rows of one m16n8k16 tile, so a
 //     loaded page is shared by the whole GQA group: S = Q K^T (mma.sync, fp32
 //     accumulate), online softmax on the S fragments in registers (quad
 //     shuffles), O += P V with V read through ldmatrix.trans.
-//   * A request/head segment that straddles warps is written as normalised
-//     fp32 partials plus base-2 LSE; the last warp to finish that segment
-//     (atomic counter per segment) merges the pieces in the same launch.
+//   * A (request, kv head) segment that straddles runs is written as
+//     normalised fp32 partials plus base-2 LSE; the last warp to finish that
+//     segment (atomic counter per segment) merges the pieces in the same launch.
 #pragma once
 
 #include "pa_common.cuh"
 
 namespace pa {
 
-template <int D>
-struct DecodeCfg {
-  static constexpr int kPanels = D / 64;           // 128-byte swizzle panels per row
-  static constexpr int kTileBytes = kPage * D * 2;  // one page-head of K (or V)
-  static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStages = (D == 64) ? 6 : 3;
-  static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kSmemBytes =
-      kDecodeWarps * kRingBytes + kDecodeWarps * kStages * 8 + 1024;
+// Shared memory the decode rings may use per CTA (tunable at build time),
+// and the stage cap.
+#ifndef PA_DECODE_RING_KB
+#define PA_DECODE_RING_KB 144
+#endif
+constexpr int kDecodeRingBudget = PA_DECODE_RING_KB * 1024;
+constexpr int kDecodeMaxStages = 8;
+// Warps per CTA (one per kv head of each group). head_dim 128 pages are
+// 4x larger per head, so that kernel keeps 8 warps to fit >= 2 stages.
+#ifndef PA_DECODE_WARPS_D64
+#define PA_DECODE_WARPS_D64 12
+#endif
+constexpr int kDecodeWarpsD64 = PA_DECODE_WARPS_D64;
+constexpr int kDecodeWarpsD128 = 8;
+
+__host__ __device__ constexpr int decode_cta_warps(int head_dim) {
+  return head_dim == 64 ? kDecodeWarpsD64 : kDecodeWarpsD128;
+}
+
+// Host-side launch geometry of the decode kernel for one cache shape.
+struct DecodeGeom {
+  int hb;            // kv heads per group (warps per group)
+  int nhb;           // head blocks per page
+  int groups_per_cta;
+  int stages;
+  int stage_bytes;   // hb * P * D * 2 (K, V) * 2 B
+  int smem_bytes;
+  int threads;       // 32 * groups_per_cta * hb
 };
 
+__host__ __device__ inline bool decode_geom(int hkv, int head_dim, DecodeGeom* g) {
+  if (hkv <= 0 || (head_dim != 64 && head_dim != 128)) return false;
+  const int hb = hkv <= 8 ? hkv : 8;
+  if (hkv % hb) return false;
+  g->hb = hb;
+  g->nhb = hkv / hb;
+  g->groups_per_cta = decode_cta_warps(head_dim) / hb;
+  if (g->groups_per_cta < 1) return false;
+  g->stage_bytes = hb * kPage * head_dim * 2 * 2;
+  int s = kDecodeRingBudget / (g->groups_per_cta * g->stage_bytes);
+  if (s > kDecodeMaxStages) s = kDecodeMaxStages;
+  if (s < 2) return false;
+  g->stages = s;
+  const int warps = g->groups_per_cta * hb;
+  // rings | full mbarriers (8 B) | release counters (4 B) | per-warp walk (2 x (S+1) ints)
+  const int aux = g->groups_per_cta * s * 8 + g->groups_per_cta * s * 4 + warps * 2 * (s + 1) * 4;
+  g->smem_bytes = g->groups_per_cta * s * g->stage_bytes + ((aux + 15) / 16) * 16 + 1024;
+  g->threads = 32 * warps;
+  return true;
+}
+
 // --------------------------------------------------------------------- plan
-// One CTA. Validates the CSR table, partitions the stream, clears the merge
-// counters. W = number of persistent warps the run kernel launches.
+// One CTA. Validates the CSR table, cuts the (request, head block, page)
+// stream into runs of Q pages for `num_groups` groups, clears the merge
+// counters.
 __global__ void decode_plan_kernel(const int32_t* __restrict__ kv_indptr,
                                    const int32_t* __restrict__ last_len, int batch, int hkv,
                                    int hq, int head_dim, int page_size, int64_t num_indices,
-                                   int num_warps, int min_per_warp, uint8_t* __restrict__ ws) {
-  const DecodeWsLayout L = decode_ws_layout(num_warps, batch, hkv, head_dim);
+                                   int num_groups, int hb, int min_per_group,
+                                   uint8_t* __restrict__ ws) {
+  const DecodeWsLayout L = decode_ws_layout(num_groups, batch, hkv, head_dim, hb);
   DecodePlanHeader* hdr = reinterpret_cast<DecodePlanHeader*>(ws + L.hdr);
-  int4* warp_start = reinterpret_cast<int4*>(ws + L.warp_start);
+  int4* unit_start = reinterpret_cast<int4*>(ws + L.unit_start);
   int32_t* empty = reinterpret_cast<int32_t*>(ws + L.empty);
   int32_t* counter = reinterpret_cast<int32_t*>(ws + L.counter);
+  const int nhb = hkv / hb;
 
   __shared__ int s_err;
   __shared__ int s_empty;
@@ -71,52 +121,54 @@ __global__ void decode_plan_kernel(const int32_t* __restrict__ kv_indptr,
   for (int i = threadIdx.x; i < batch * hkv; i += blockDim.x) counter[i] = 0;
   const int first = kv_indptr[0];
   const long long last_ptr = kv_indptr[batch];
-  const long long total_ll = static_cast<long long>(hkv) * last_ptr;
-  if (first != 0 || last_ptr > num_indices || total_ll > 0x7fffffffLL) {
+  const long long total_ll = static_cast<long long>(nhb) * last_ptr;
+  if (first != 0 || last_ptr > num_indices || total_ll > 0x3fffffffLL) {
     if (threadIdx.x == 0) atomicOr(&s_err, 1);
   }
   __syncthreads();
   const bool err = s_err != 0;
   const int total = err ? 0 : static_cast<int>(total_ll);
-  int q = (total + num_warps - 1) / num_warps;
-  q = max(q, min_per_warp);
-  for (int w = threadIdx.x; w < num_warps; w += blockDim.x) {
+  int q = (total + num_groups - 1) / num_groups;
+  q = max(q, min_per_group);
+  for (int w = threadIdx.x; w < num_groups; w += blockDim.x) {
     const long long s0 = static_cast<long long>(w) * q;
     int4 st = make_int4(0, 0, 0, 0);
     if (s0 < total) {
-      // Largest b with hkv * kv_indptr[b] <= s0 (empty requests are skipped
-      // because their start equals the next request's start).
-      int lo = 0, hi = batch;  // invariant: hkv*indptr[lo] <= s0 < hkv*indptr[hi]
+      // Largest b with nhb * kv_indptr[b] <= s0; requests without pages are
+      // skipped because their start equals the next request's start.
+      int lo = 0, hi = batch;  // invariant: nhb*indptr[lo] <= s0 < nhb*indptr[hi]
       while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
-        if (static_cast<long long>(hkv) * kv_indptr[mid] <= s0) lo = mid; else hi = mid;
+        if (static_cast<long long>(nhb) * kv_indptr[mid] <= s0) lo = mid; else hi = mid;
       }
       const int base = kv_indptr[lo];
       const int n = kv_indptr[lo + 1] - base;
-      const int off = static_cast<int>(s0 - static_cast<long long>(hkv) * base);
+      const int off = static_cast<int>(s0 - static_cast<long long>(nhb) * base);
       st = make_int4(lo, off / n, off % n, 0);
     }
-    warp_start[w] = st;
+    unit_start[w] = st;
   }
   if (threadIdx.x == 0) {
     hdr->status = err ? PA_ERR_DEVICE_CHECK : PA_OK;
     hdr->total = total;
-    hdr->per_warp = q;
-    hdr->num_warps = num_warps;
+    hdr->per_unit = q;
+    hdr->num_units = num_groups;
     hdr->batch_size = batch;
     hdr->num_kv_heads = hkv;
     hdr->num_qo_heads = hq;
     hdr->head_dim = head_dim;
     hdr->page_size = page_size;
     hdr->num_empty = err ? 0 : s_empty;
+    hdr->heads_per_unit = hb;
     hdr->magic = kDecodeMagic;
     if (err) set_status(PA_ERR_DEVICE_CHECK);
   }
 }
 
 // ---------------------------------------------------------------------- run
+// Position in the work stream: request b, head block hblk, page j of n.
 struct StreamCursor {
-  int b, h, j, n, base;
+  int b, hblk, j, n, base;
 };
 
 __device__ __forceinline__ void cursor_load(StreamCursor& c, const int32_t* indptr) {
@@ -125,47 +177,109 @@ __device__ __forceinline__ void cursor_load(StreamCursor& c, const int32_t* indp
 }
 
 // Moves to the next stream position; must only be called when one exists.
-__device__ __forceinline__ void cursor_next(StreamCursor& c, const int32_t* indptr, int hkv) {
+__device__ __forceinline__ void cursor_next(StreamCursor& c, const int32_t* indptr, int nhb) {
   if (++c.j < c.n) return;
   c.j = 0;
-  if (++c.h < hkv) return;
-  c.h = 0;
+  if (++c.hblk < nhb) return;
+  c.hblk = 0;
   do {
     ++c.b;
     cursor_load(c, indptr);
   } while (c.n == 0);
 }
 
+// Log-sum-exp merge of every piece of segment (request b, kv head `head`):
+// o = sum_u 2^(lse_u - max) o_u / sum_u 2^(lse_u - max). The G x D outputs
+// are spread over the lanes in float4 granules; each granule streams its
+// pieces' LSEs and partial rows with independent loads (online max), so a
+// merge costs a couple of L2 round trips rather than one per row.
 template <typename T, int D>
-__global__ void __launch_bounds__(kDecodeWarps * 32, 1)
+__device__ __noinline__ void merge_segment(const float* part_lse, const float* part_o, T* out,
+                                           float* lse, int* counter, int G, int hq, int hkv,
+                                           int Q, int HB, int hh, int b, int head, int seg_start,
+                                           int seg_len, int lane) {
+  const int u0 = seg_start / Q, u1 = (seg_start + seg_len - 1) / Q;
+  T* ob = out + (static_cast<size_t>(b) * hq + head * G) * D;
+  constexpr int C4 = D / 4;
+  for (int it = lane; it < G * C4; it += 32) {
+    const int r = it / C4, c = (it - r * C4) * 4;
+    float m = -INFINITY, w = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = u0; u <= u1; ++u) {
+      const size_t sl = static_cast<size_t>((u * 2 + (seg_start <= u * Q ? 0 : 1)) * HB + hh);
+      const float l = __ldcg(part_lse + sl * kMaxGroup + r);
+      const float4 v =
+          __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
+      const float mn = fmaxf(m, l);
+      const float sc = ex2(m - mn), wt = ex2(l - mn);
+      acc.x = acc.x * sc + wt * v.x;
+      acc.y = acc.y * sc + wt * v.y;
+      acc.z = acc.z * sc + wt * v.z;
+      acc.w = acc.w * sc + wt * v.w;
+      w = w * sc + wt;
+      m = mn;
+    }
+    const float inv = 1.f / w;
+    uint2 packed;
+    packed.x = pack2<T>(acc.x * inv, acc.y * inv);
+    packed.y = pack2<T>(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(ob + r * D + c) = packed;
+    if (lse != nullptr && c == 0) lse[static_cast<size_t>(b) * hq + head * G + r] = m + lg2(w);
+  }
+  __syncwarp();
+  if (lane == 0) counter[b * hkv + head] = 0;  // ready for the next launch
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
     decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const DecodeParams p) {
-  using C = DecodeCfg<D>;
-  constexpr int NT = D / 8;   // 8-wide column tiles of O
-  constexpr int KS = D / 16;  // 16-deep k steps of Q K^T
-  constexpr int S = C::kStages;
+  constexpr int NT = D / 8;       // 8-wide column tiles of O
+  constexpr int KS = D / 16;      // 16-deep k steps of Q K^T
+  constexpr int PANELS = D / 64;  // 128-byte swizzle panels per row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
 
+  const int HB = p.hb, NHB = p.nhb, S = p.stages, SB = p.stage_bytes, GPC = p.groups_per_cta;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gid = lane >> 2, tig = lane & 3;
-  const int W = gridDim.x * kDecodeWarps;
-  const int gw = blockIdx.x * kDecodeWarps + warp;
+  const int nwarps = GPC * HB;
+  const int g_local = warp / HB, hh = warp - g_local * HB;
+  const int num_groups = gridDim.x * GPC;
+  const int grp = blockIdx.x * GPC + g_local;
+  const int gw = blockIdx.x * nwarps + warp;  // global warp id
+  const int total_warps = gridDim.x * nwarps;
   const DecodePlanHeader* hdr = p.hdr;
 
-  if (hdr->magic != kDecodeMagic || hdr->num_warps != W || hdr->batch_size != p.batch_size ||
-      hdr->num_kv_heads != p.num_kv_heads || hdr->num_qo_heads != p.num_qo_heads ||
-      hdr->head_dim != D) {
+  // Shared memory: rings, full barriers, release counters, per-warp walk.
+  uint8_t* rings = smem;
+  uint64_t* fullb = reinterpret_cast<uint64_t*>(rings + GPC * S * SB);
+  int* relc = reinterpret_cast<int*>(fullb + GPC * S);
+  int* walk_all = relc + GPC * S;
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
+    for (int s = 0; s < GPC * S; ++s) {
+      mbar_init(&fullb[s], 1);
+      relc[s] = 0;
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (hdr->magic != kDecodeMagic || hdr->num_units != num_groups ||
+      hdr->batch_size != p.batch_size || hdr->num_kv_heads != p.num_kv_heads ||
+      hdr->num_qo_heads != p.num_qo_heads || hdr->head_dim != D || hdr->heads_per_unit != HB) {
     if (gw == 0 && lane == 0) set_status(PA_ERR_NOT_PLANNED);
     return;
   }
   if (hdr->status != PA_OK) return;
-  const int Q = hdr->per_warp, total = hdr->total, hkv = p.num_kv_heads, G = p.group;
+  const int Q = hdr->per_unit, total = hdr->total, hkv = p.num_kv_heads, G = p.group;
   const int hq = p.num_qo_heads;
   T* out = reinterpret_cast<T*>(p.out);
 
   // Requests without pages produce zeros (and LSE = -inf).
-  for (int e = gw; e < hdr->num_empty; e += W) {
+  for (int e = gw; e < hdr->num_empty; e += total_warps) {
     const int b = p.empty[e];
     for (int i = lane; i < hq * D / 8; i += 32)
       reinterpret_cast<uint4*>(out + static_cast<size_t>(b) * hq * D)[i] = make_uint4(0, 0, 0, 0);
@@ -173,66 +287,91 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       for (int i = lane; i < hq; i += 32) p.lse[static_cast<size_t>(b) * hq + i] = -INFINITY;
   }
 
-  const int s0 = gw * Q;
+  const int s0 = grp * Q;
   if (s0 >= total) return;
   const int cnt = min(Q, total - s0);
 
-  uint8_t* ring = smem + warp * C::kRingBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeWarps * C::kRingBytes) + warp * S;
-  if (lane == 0) {
-    prefetch_tensormap(&kmap);
-    prefetch_tensormap(&vmap);
-#pragma unroll
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
+  uint8_t* ring = rings + g_local * S * SB;
+  uint64_t* bars = fullb + g_local * S;
+  int* rel = relc + g_local * S;
+  int* walk = walk_all + warp * 2 * (S + 1);
 
-  const int4 st = p.warp_start[gw];
+  const int4 st = p.unit_start[grp];
   StreamCursor pc;
   pc.b = st.x;
-  pc.h = st.y;
+  pc.hblk = st.y;
   pc.j = st.z;
   cursor_load(pc, p.kv_indptr);
   StreamCursor cc = pc;
+  const int panel_bytes = HB * 2048;
 
-  // Lane 0 fills stage `stage` with the K and V tiles of cursor position c.
-  auto issue = [&](int stage, const StreamCursor& c) {
-    if (lane == 0) {
-      int page = __ldg(p.kv_indices + c.base + c.j);
-      if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
-        set_status(PA_ERR_DEVICE_CHECK);
-        page = 0;
-      }
-      uint8_t* dst = ring + stage * C::kStageBytes;
-      mbar_arrive_expect_tx(&bars[stage], C::kStageBytes);
-      const int c1 = p.heads_inner ? c.h : 0, c2 = p.heads_inner ? 0 : c.h;
+  // Fills stage `stage` with page `page` of head block `hblk` (one thread).
+  auto issue = [&](int stage, int page, int hblk) {
+    if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
+      set_status(PA_ERR_DEVICE_CHECK);
+      page = 0;
+    }
+    uint8_t* dst = ring + stage * SB;
+    mbar_arrive_expect_tx(&bars[stage], SB);
+    const int h0 = hblk * HB;
+    const int c1 = p.heads_inner ? h0 : 0, c2 = p.heads_inner ? 0 : h0;
 #pragma unroll
-      for (int pn = 0; pn < C::kPanels; ++pn) {
-        tma_load_4d(dst + pn * 2048, &kmap, &bars[stage], pn * 64, c1, c2, page);
-        tma_load_4d(dst + C::kTileBytes + pn * 2048, &vmap, &bars[stage], pn * 64, c1, c2, page);
-      }
+    for (int pn = 0; pn < PANELS; ++pn) {
+      tma_load_4d(dst + pn * panel_bytes, &kmap, &bars[stage], pn * 64, c1, c2, page);
+      tma_load_4d(dst + (PANELS + pn) * panel_bytes, &vmap, &bars[stage], pn * 64, c1, c2, page);
     }
   };
 
+  // Prologue: every warp of the group walks the first min(S + 1, cnt)
+  // positions (one page-id round trip, lane-parallel); warp 0 of the group
+  // fills the ring. Position S, if any, is the first refill: its id is kept
+  // in pf_page so each refill issues with an id loaded one iteration early.
   const int npro = min(S, cnt);
+  const int nwalk = min(S + 1, cnt);
+  if (lane == 0) {
+    for (int k = 0; k < nwalk; ++k) {
+      if (k > 0) cursor_next(pc, p.kv_indptr, NHB);
+      walk[k] = pc.base + pc.j;
+      walk[S + 1 + k] = pc.hblk;
+    }
+  }
+  __syncwarp();
+  int my_page = 0, my_hb = 0;
+  if (lane < nwalk) {
+    my_page = __ldg(p.kv_indices + walk[lane]);
+    my_hb = walk[S + 1 + lane];
+  }
+  int pf_page = __shfl_sync(0xffffffffu, my_page, npro < cnt ? npro : 0);
+  int pf_hb = __shfl_sync(0xffffffffu, my_hb, npro < cnt ? npro : 0);
   for (int k = 0; k < npro; ++k) {
-    if (k > 0) cursor_next(pc, p.kv_indptr, hkv);
-    issue(k, pc);
+    const int pg = __shfl_sync(0xffffffffu, my_page, k);
+    const int hbk = __shfl_sync(0xffffffffu, my_hb, k);
+    if (hh == 0 && lane == 0) issue(k, pg, hbk);
   }
 
   const T* qbase = reinterpret_cast<const T*>(p.q);
   uint32_t qf[KS][4];
   float o[NT][4];
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  int seg_start = 0, last_len = kPage;
+  int seg_start = 0, last_len = kPage, head = 0;
   const bool row0 = gid < G, row1 = gid + 8 < G;
+  // Row of token r of this warp's head inside a panel of the stage.
+  const int row_mul = p.heads_inner ? HB : 1;
+  const int row_add = p.heads_inner ? hh : hh * kPage;
 
+  // Split segments whose piece this warp wrote (at most the first and the
+  // last segment of its run); counted and merged after the loop.
+  int n_pend = 0;
+  int pend_b[2] = {0, 0}, pend_head[2] = {0, 0}, pend_seg[2] = {0, 0}, pend_len[2] = {0, 0};
+
+  int stage = 0;
+  uint32_t phase = 0;
   for (int i = 0; i < cnt; ++i) {
     if (i == 0 || cc.j == 0) {
       // New (request, kv head) segment: load the group's q rows as A fragments.
+      head = cc.hblk * HB + hh;
       const T* qh = qbase + static_cast<int64_t>(cc.b) * p.q_stride_n +
-                    static_cast<int64_t>(cc.h * G) * p.q_stride_h;
+                    static_cast<int64_t>(head * G) * p.q_stride_h;
       const T* q0 = qh + static_cast<int64_t>(gid) * p.q_stride_h;
       const T* q1 = qh + static_cast<int64_t>(gid + 8) * p.q_stride_h;
 #pragma unroll
@@ -247,20 +386,17 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
       m0 = m1 = -INFINITY;
       l0 = l1 = 0.f;
-      seg_start = hkv * cc.base + cc.h * cc.n;
+      seg_start = NHB * cc.base + cc.hblk * cc.n;
       last_len = __ldg(p.kv_last_page_len + cc.b);
     }
 
-    const int stage = i % S;
-    if (!mbar_wait(&bars[stage], (i / S) & 1)) {
+    if (!mbar_wait(&bars[stage], phase)) {
       set_status(PA_ERR_TIMEOUT);
-      // Give the copies still in flight a bounded chance to land, then leave.
-      for (int k = i + 1; k < min(i + S, cnt); ++k) mbar_wait(&bars[k % S], (k / S) & 1);
       return;
     }
-    uint8_t* kst = ring + stage * C::kStageBytes;
+    uint8_t* kst = ring + stage * SB;
     const uint32_t kb = smem_u32(kst);
-    const uint32_t vb = kb + C::kTileBytes;
+    const uint32_t vb = kb + PANELS * panel_bytes;
     const int valid = (cc.j == cc.n - 1) ? last_len : kPage;
 
     // ---- S = Q K^T over the 16 keys of this page
@@ -268,14 +404,14 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 #pragma unroll
     for (int t = 0; t < 2; ++t) s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
     {
-      const int krow = (lane & 7) + ((lane >> 4) & 1) * 8;
+      const int krow = ((lane & 7) + ((lane >> 4) & 1) * 8) * row_mul + row_add;
       const int khalf = (lane >> 3) & 1;
 #pragma unroll
       for (int kk = 0; kk < KS; ++kk) {
         const int panel = kk >> 2;
         const int chunk = ((kk & 3) << 1) + khalf;
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(kb + panel * 2048 + sw128(krow, chunk), b0, b1, b2, b3);
+        ldsm_x4(kb + panel * panel_bytes + sw128(krow, chunk), b0, b1, b2, b3);
         Mma16816<T>::run(s[0], qf[kk], b0, b1);
         Mma16816<T>::run(s[1], qf[kk], b2, b3);
       }
@@ -324,16 +460,15 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
     pa[2] = pack2<T>(pr[1][0], pr[1][1]);
     pa[3] = pack2<T>(pr[1][2], pr[1][3]);
 
-    // Slots past the last key hold stale pool bytes; zero those V rows so a
-    // non-finite value there cannot reach O through 0 * Inf.
+    // Slots past the last key hold stale pool bytes; zero this head's V rows
+    // there so a non-finite value cannot reach O through 0 * Inf.
     if (valid < kPage) {
-      uint8_t* vst = kst + C::kTileBytes;
-      const int per_row = C::kPanels * 8;
-      for (int idx = lane; idx < (kPage - valid) * per_row; idx += 32) {
-        const int r = valid + idx / per_row;
-        const int rem = idx % per_row;
-        *reinterpret_cast<uint4*>(vst + (rem >> 3) * 2048 + r * 128 + (rem & 7) * 16) =
-            make_uint4(0, 0, 0, 0);
+      uint8_t* vst = kst + PANELS * panel_bytes;
+      for (int idx = lane; idx < (kPage - valid) * PANELS * 8; idx += 32) {
+        const int r = valid + idx / (PANELS * 8);
+        const int rem = idx % (PANELS * 8);
+        *reinterpret_cast<uint4*>(vst + (rem >> 3) * panel_bytes + (r * row_mul + row_add) * 128 +
+                                  (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async();
       __syncwarp();
@@ -341,24 +476,35 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 
     // ---- O += P V
     {
-      const int vrow = (lane & 7) + ((lane >> 3) & 1) * 8;
+      const int vrow = ((lane & 7) + ((lane >> 3) & 1) * 8) * row_mul + row_add;
       const int vhalf = lane >> 4;
 #pragma unroll
       for (int np = 0; np < NT / 2; ++np) {
         const int panel = np >> 2;
         const int chunk = ((np & 3) << 1) + vhalf;
         uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(vb + panel * 2048 + sw128(vrow, chunk), v0, v1, v2, v3);
+        ldsm_x4_t(vb + panel * panel_bytes + sw128(vrow, chunk), v0, v1, v2, v3);
         Mma16816<T>::run(o[2 * np], pa, v0, v1);
         Mma16816<T>::run(o[2 * np + 1], pa, v2, v3);
       }
     }
     __syncwarp();
 
-    // Refill the stage just consumed with the page S positions ahead.
-    if (i + S < cnt) {
-      cursor_next(pc, p.kv_indptr, hkv);
-      issue(stage, pc);
+    // Release the stage. The last warp of the group to release it refills it
+    // with the page S positions ahead; every warp then moves its copy of the
+    // refill cursor and loads the next page id (used next iteration).
+    if (lane == 0) {
+      __threadfence_block();
+      const int old = atomicAdd(&rel[stage], 1);
+      if ((old + 1) % HB == 0 && i + S < cnt) {
+        __threadfence_block();
+        issue(stage, pf_page, pf_hb);
+      }
+      if (i + S + 1 < cnt) {
+        cursor_next(pc, p.kv_indptr, NHB);
+        pf_page = __ldg(p.kv_indices + pc.base + pc.j);
+        pf_hb = pc.hblk;
+      }
     }
 
     // ---- end of this warp's piece of the segment
@@ -370,7 +516,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
       const float inv0 = 1.f / l0, inv1 = 1.f / l1;
       const int seg_end = seg_start + cc.n;
       const bool split = seg_start < s0 || seg_end > s0 + cnt;
-      const int head0 = cc.h * G;
+      const int head0 = head * G;
       if (!split) {
         T* ob = out + (static_cast<size_t>(cc.b) * hq + head0) * D;
 #pragma unroll
@@ -389,7 +535,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           if (row1) lb[gid + 8] = m1 + lg2(l1);
         }
       } else {
-        const int slot = gw * 2 + (seg_start <= s0 ? 0 : 1);
+        const int slot = ((grp * 2 + (seg_start <= s0 ? 0 : 1)) * HB) + hh;
         float* po = p.part_o + static_cast<size_t>(slot) * kMaxGroup * D;
         float* pl = p.part_lse + static_cast<size_t>(slot) * kMaxGroup;
 #pragma unroll
@@ -404,60 +550,41 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
           if (row0) __stcg(pl + gid, m0 + lg2(l0));
           if (row1) __stcg(pl + gid + 8, m1 + lg2(l1));
         }
-        __threadfence();
-        __syncwarp();
-        int* cnt_ptr = p.counter + cc.b * hkv + cc.h;
-        int old = 0;
-        if (lane == 0) old = atomicAdd(cnt_ptr, 1);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        const int w0 = seg_start / Q, w1 = (seg_end - 1) / Q;
-        if (old == w1 - w0) {
-          // Last piece of this segment to finish: merge all pieces.
-          __threadfence();
-          constexpr int E = D / 32;
-          T* ob = out + (static_cast<size_t>(cc.b) * hq + head0) * D;
-          for (int r = 0; r < G; ++r) {
-            float lmax = -INFINITY;
-            for (int w = w0; w <= w1; ++w) {
-              const int sl = w * 2 + (seg_start <= w * Q ? 0 : 1);
-              lmax = fmaxf(lmax, __ldcg(p.part_lse + static_cast<size_t>(sl) * kMaxGroup + r));
-            }
-            float acc[E];
-#pragma unroll
-            for (int e = 0; e < E; ++e) acc[e] = 0.f;
-            float wsum = 0.f;
-            for (int w = w0; w <= w1; ++w) {
-              const int sl = w * 2 + (seg_start <= w * Q ? 0 : 1);
-              const float wt =
-                  ex2(__ldcg(p.part_lse + static_cast<size_t>(sl) * kMaxGroup + r) - lmax);
-              wsum += wt;
-              const float* src = p.part_o + (static_cast<size_t>(sl) * kMaxGroup + r) * D + lane * E;
-              if constexpr (E == 2) {
-                const float2 v = __ldcg(reinterpret_cast<const float2*>(src));
-                acc[0] += wt * v.x;
-                acc[1] += wt * v.y;
-              } else {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(src));
-                acc[0] += wt * v.x;
-                acc[1] += wt * v.y;
-                acc[2] += wt * v.z;
-                acc[3] += wt * v.w;
-              }
-            }
-            const float winv = 1.f / wsum;
-            T* dst = ob + r * D + lane * E;
-#pragma unroll
-            for (int e = 0; e < E; e += 2)
-              *reinterpret_cast<uint32_t*>(dst + e) = pack2<T>(acc[e] * winv, acc[e + 1] * winv);
-            if (p.lse != nullptr && lane == 0)
-              p.lse[static_cast<size_t>(cc.b) * hq + head0 + r] = lmax + lg2(wsum);
-          }
-          if (lane == 0) *cnt_ptr = 0;  // ready for the next launch on this plan
+        // Counted (and merged, if this piece turns out to be the last one)
+        // after the main loop, so no fence or atomic stalls this group's ring.
+        if (n_pend < 2) {
+          pend_b[n_pend] = cc.b;
+          pend_head[n_pend] = head;
+          pend_seg[n_pend] = seg_start;
+          pend_len[n_pend] = cc.n;
+          ++n_pend;
         }
       }
     }
 
-    if (i + 1 < cnt) cursor_next(cc, p.kv_indptr, hkv);
+    if (i + 1 < cnt) cursor_next(cc, p.kv_indptr, NHB);
+    if (++stage == S) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+
+  if (n_pend > 0) {
+    // Publish this warp's partials, then count its pieces; the warp that
+    // completes a segment's count merges that segment.
+    __threadfence();
+    __syncwarp();
+    for (int k = 0; k < n_pend; ++k) {
+      int old = 0;
+      if (lane == 0) old = atomicAdd(p.counter + pend_b[k] * hkv + pend_head[k], 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      const int u0 = pend_seg[k] / Q, u1 = (pend_seg[k] + pend_len[k] - 1) / Q;
+      if (old == u1 - u0) {
+        __threadfence();
+        merge_segment<T, D>(p.part_lse, p.part_o, out, p.lse, p.counter, G, hq, hkv, Q, HB, hh,
+                            pend_b[k], pend_head[k], pend_seg[k], pend_len[k], lane);
+      }
+    }
   }
 }
 

@@ -13,7 +13,6 @@ constexpr int kPage = 16;
 // Largest GQA group (q heads per kv head) one decode warp tile holds: the
 // 16 rows of an m16n8k16 A fragment.
 constexpr int kMaxGroup = 16;
-constexpr int kDecodeWarps = 8;
 constexpr int32_t kDecodeMagic = 0x50414431;   // "PAD1"
 constexpr int32_t kPrefillMagic = 0x50415031;  // "PAP1"
 
@@ -35,42 +34,43 @@ __device__ __forceinline__ T* align1024(T* p) {
 // ------------------------------------------------------------------ decode
 struct DecodePlanHeader {
   int32_t magic;
-  int32_t status;        // PA_OK, or PA_ERR_DEVICE_CHECK when the table is malformed
-  int32_t total;         // page-heads in the stream = H_kv * kv_indptr[B]
-  int32_t per_warp;      // Q: page-heads per persistent warp
-  int32_t num_warps;     // W the partition was built for
+  int32_t status;          // PA_OK, or PA_ERR_DEVICE_CHECK when the table is malformed
+  int32_t total;           // pages in the stream = head blocks * kv_indptr[B]
+  int32_t per_unit;        // Q: pages per group
+  int32_t num_units;       // groups the partition was built for
   int32_t batch_size;
   int32_t num_kv_heads;
   int32_t num_qo_heads;
   int32_t head_dim;
   int32_t page_size;
-  int32_t num_empty;     // requests with zero pages (their output is zero)
-  int32_t reserved[5];
+  int32_t num_empty;       // requests with zero pages (their output is zero)
+  int32_t heads_per_unit;  // kv heads a group covers (one warp each)
+  int32_t reserved[4];
 };
 
-// Byte offsets inside the caller's workspace. The stream of work is the
-// concatenation over requests b and kv heads h of that request's pages;
-// warp w owns stream positions [w*Q, (w+1)*Q).
+// Byte offsets inside the caller's workspace. The stream of work is every
+// (request b, head block, page j); group u owns positions [u*Q, (u+1)*Q).
 struct DecodeWsLayout {
-  size_t hdr, warp_start, empty, counter, part_lse, part_o, total;
+  size_t hdr, unit_start, empty, counter, part_lse, part_o, total;
 };
 
-__host__ __device__ inline DecodeWsLayout decode_ws_layout(int num_warps, int batch, int hkv,
-                                                           int head_dim) {
+__host__ __device__ inline DecodeWsLayout decode_ws_layout(int num_units, int batch, int hkv,
+                                                           int head_dim, int heads_per_unit) {
   DecodeWsLayout L;
+  const size_t slots = static_cast<size_t>(num_units) * 2 * heads_per_unit;
   size_t o = 0;
   L.hdr = o;
   o = align256(o + sizeof(DecodePlanHeader));
-  L.warp_start = o;  // int4 {b, h, j, 0} of each warp's first page
-  o = align256(o + sizeof(int4) * static_cast<size_t>(num_warps));
+  L.unit_start = o;  // int4 {b, head block, j, 0} of each group's first page
+  o = align256(o + sizeof(int4) * static_cast<size_t>(num_units));
   L.empty = o;  // int32 list of requests without pages
   o = align256(o + 4 * static_cast<size_t>(batch));
   L.counter = o;  // int32 per (request, kv head): pieces finished this launch
   o = align256(o + 4 * static_cast<size_t>(batch) * hkv);
-  L.part_lse = o;  // float [W][2][kMaxGroup]: base-2 LSE of split pieces
-  o = align256(o + 4 * static_cast<size_t>(num_warps) * 2 * kMaxGroup);
-  L.part_o = o;  // float [W][2][kMaxGroup][D]: normalised output of split pieces
-  o = align256(o + 4 * static_cast<size_t>(num_warps) * 2 * kMaxGroup * head_dim);
+  L.part_lse = o;  // float [units][2][heads][kMaxGroup]: base-2 LSE of split pieces
+  o = align256(o + 4 * slots * kMaxGroup);
+  L.part_o = o;  // float [units][2][heads][kMaxGroup][D]: normalised split outputs
+  o = align256(o + 4 * slots * kMaxGroup * head_dim);
   L.total = o;
   return L;
 }
@@ -87,8 +87,10 @@ struct DecodeParams {
   int64_t num_pages;
   int32_t heads_inner;  // tensor-map dim order (D, H, P, pages) instead of (D, P, H, pages)
   float scale_log2;     // sm_scale * log2(e)
+  // launch geometry (DecodeGeom)
+  int32_t hb, nhb, groups_per_cta, stages, stage_bytes;
   const DecodePlanHeader* hdr;
-  const int4* warp_start;
+  const int4* unit_start;
   const int32_t* empty;
   int32_t* counter;
   float* part_lse;
