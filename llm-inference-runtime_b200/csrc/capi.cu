@@ -3,6 +3,7 @@
 // Single translation unit: every kernel header is included here so device
 // globals (the status word) need no relocatable device code.
 #include <atomic>
+#include <type_traits>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -154,6 +155,39 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
     allowed[dev].store(sh.g.smem_bytes, std::memory_order_relaxed);
   }
   decode_kernel<T, D><<<sh.ctas, sh.g.threads, sh.g.smem_bytes, stream>>>(km, vm, prm);
+  return launch_status();
+}
+
+// 3-D map over q [tokens, heads, dim] (strides in elements), box (64 dims,
+// g heads, qt tokens): the box lands as 128 rows (token-major, head-minor)
+// of 128 bytes, 128-byte swizzled — the K-major A tile of S = Q K^T.
+int encode_q_map(CUtensorMap* map, const void* q, int64_t stride_n, int64_t stride_h,
+                 int64_t total_qo, int hq, int head_dim, int g, int qt, int dtype) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return PA_ERR_CUDA;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(hq),
+                              static_cast<cuuint64_t>(total_qo)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(stride_h) * 2,
+                                 static_cast<cuuint64_t>(stride_n) * 2};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(g), static_cast<cuuint32_t>(qt)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 3, const_cast<void*>(q), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PA_OK : PA_ERR_INVALID_ARGUMENT;
+}
+
+template <typename T, int D>
+int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
+                   const PrefillParams& prm, int64_t grid, int dev, cudaStream_t stream) {
+  static std::atomic<uint64_t> done{0};
+  constexpr int smem = PfCfg<D>::kSmemBytes;
+  if (allow_smem(prefill_kernel<T, D>, smem, &done, dev) != cudaSuccess) return PA_ERR_CUDA;
+  if (grid <= 0) return PA_OK;
+  if (grid > 0x7fffffffLL) return PA_ERR_INVALID_ARGUMENT;
+  prefill_kernel<T, D><<<static_cast<unsigned>(grid), kPfThreads, smem, stream>>>(qm, km, vm, prm);
   return launch_status();
 }
 
@@ -408,7 +442,12 @@ int pa_merge_states(const void* v, const float* s, int32_t seq_len, int32_t num_
 
 size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int32_t num_qo_heads,
                                   int32_t num_kv_heads, int32_t head_dim) {
-  return prefill_workspace_bytes(batch_size, max_total_qo, num_qo_heads, num_kv_heads, head_dim);
+  if (batch_size <= 0 || max_total_qo < 0 || num_kv_heads <= 0 || num_qo_heads <= 0 ||
+      num_qo_heads % num_kv_heads || head_dim <= 0)
+    return 0;
+  const int qt = prefill_qt(num_qo_heads / num_kv_heads);
+  if (qt == 0) return 0;
+  return prefill_ws_layout(prefill_max_items(batch_size, max_total_qo, num_kv_heads, qt)).total;
 }
 
 int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
@@ -416,9 +455,23 @@ int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
                     int64_t num_kv_indices, int32_t num_qo_heads, int32_t num_kv_heads,
                     int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
                     void* stream) {
-  return prefill_plan(qo_indptr, kv_indptr, kv_last_page_len, batch_size, total_qo,
-                      num_kv_indices, num_qo_heads, num_kv_heads, head_dim, page_size, workspace,
-                      workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (qo_indptr == nullptr || kv_indptr == nullptr || kv_last_page_len == nullptr ||
+      workspace == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size <= 0 || total_qo < 0 || num_kv_indices < 0 || num_qo_heads <= 0 ||
+      num_kv_heads <= 0 || num_qo_heads % num_kv_heads)
+    return PA_ERR_INVALID_ARGUMENT;
+  const int qt = prefill_qt(num_qo_heads / num_kv_heads);
+  if (qt == 0) return PA_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128) return PA_ERR_UNSUPPORTED;
+  if (page_size != kPage) return PA_ERR_UNSUPPORTED;
+  if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
+  const int64_t max_items = prefill_max_items(batch_size, total_qo, num_kv_heads, qt);
+  if (prefill_ws_layout(max_items).total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  prefill_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      qo_indptr, kv_indptr, kv_last_page_len, batch_size, total_qo, num_kv_indices, num_qo_heads,
+      num_kv_heads, head_dim, page_size, qt, max_items, static_cast<uint8_t*>(workspace));
+  return launch_status();
 }
 
 int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
@@ -428,9 +481,56 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
                    size_t workspace_bytes, void* out, float* lse, void* stream) {
   int st = check_cache(cache);
   if (st != PA_OK) return st;
-  return prefill_run(q, q_stride_n, q_stride_h, *cache, qo_indptr, kv_indices, kv_indptr,
-                     kv_last_page_len, batch_size, total_qo, num_qo_heads, causal, sm_scale,
-                     workspace, workspace_bytes, out, lse, static_cast<cudaStream_t>(stream));
+  if (q == nullptr || out == nullptr || qo_indptr == nullptr || kv_indices == nullptr ||
+      kv_indptr == nullptr || kv_last_page_len == nullptr || workspace == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size <= 0 || total_qo < 0 || num_qo_heads <= 0) return PA_ERR_INVALID_ARGUMENT;
+  const int hkv = cache->num_kv_heads, D = cache->head_dim;
+  if (num_qo_heads % hkv) return PA_ERR_INVALID_ARGUMENT;
+  const int G = num_qo_heads / hkv;
+  const int qt = prefill_qt(G);
+  if (qt == 0) return PA_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return PA_ERR_UNSUPPORTED;
+  if (cache->page_size != kPage) return PA_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(out) || q_stride_n % 8 || q_stride_h % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (total_qo == 0) return PA_OK;
+  const int64_t max_items = prefill_max_items(batch_size, total_qo, hkv, qt);
+  const PrefillWsLayout L = prefill_ws_layout(max_items);
+  if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  CUtensorMap qm, km, vm;
+  if ((st = encode_q_map(&qm, q, q_stride_n, q_stride_h, total_qo, num_qo_heads, D, G, qt,
+                         cache->dtype)) != PA_OK)
+    return st;
+  if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage, 1)) != PA_OK) return st;
+  if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage, 1)) != PA_OK) return st;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  PrefillParams p;
+  p.out = out;
+  p.lse = lse;
+  p.qo_indptr = qo_indptr;
+  p.kv_indptr = kv_indptr;
+  p.kv_indices = kv_indices;
+  p.kv_last_page_len = kv_last_page_len;
+  p.batch_size = batch_size;
+  p.num_qo_heads = num_qo_heads;
+  p.num_kv_heads = hkv;
+  p.group = G;
+  p.qt = qt;
+  p.causal = causal ? 1 : 0;
+  p.num_pages = cache->num_pages;
+  p.heads_inner = heads_inner(*cache) ? 1 : 0;
+  const float scale = sm_scale > 0.f ? sm_scale : 1.0f / std::sqrt(static_cast<float>(D));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.hdr = reinterpret_cast<const PrefillPlanHeader*>(ws + L.hdr);
+  p.items = reinterpret_cast<const int4*>(ws + L.items);
+  const int dev = current_device();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cache->dtype == PA_DTYPE_BF16)
+    return D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, p, max_items, dev, s)
+                   : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, p, max_items, dev, s);
+  return D == 64 ? launch_prefill<__half, 64>(qm, km, vm, p, max_items, dev, s)
+                 : launch_prefill<__half, 128>(qm, km, vm, p, max_items, dev, s);
 }
 
 }  // extern "C"
