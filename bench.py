@@ -1,7 +1,7 @@
 """Benchmark of the paged-decode attention path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2|cfg5]
+                    [--workload cfg2|cfg3|cfg5]
 
 Metric: paged-decode attention HBM GB/s (fraction of the
 measured HBM peak) and decode tok/s, at 1/2/4/8 B200.
@@ -144,6 +144,8 @@ class ClockSampler:
 
 def _workload(args):
     wl = importlib.import_module(PKG + ".workloads")
+    if args.workload == "cfg3":
+        return wl, wl.LLAMA3_8B, 128, 256, 4096, 1, "cfg3 chunked-prefill mixed batch (decode part)"
     if args.workload == "cfg5":
         return wl, wl.LLAMA3_8B, 512, 8192, 32768, 1, "cfg5 long-context split-KV decode"
     return wl, wl.TINYLLAMA, 256, 1024, 4096, 22, "cfg2 TinyLlama-1.1B decode step attention"
@@ -331,6 +333,118 @@ def _traffic_from_profile(bytes_decode: int):
     return int(d["dram_bytes_per_launch"] * bytes_decode / d["algorithmic_bytes_per_launch"])
 
 
+# --------------------------------------------------------------- cfg3
+def run_mixed(args):
+    """Configuration 3: one Llama-3-8B attention layer serving a mixed step —
+    16 prefill chunks of 512 rows over cached prefixes U[0, 2048] (causal,
+    tcgen05 prefill kernel) and 128 decode rows with contexts U[256, 4096]
+    (decode kernel), both on the same pool. Requests are sharded round-robin
+    (weak scaling: the whole mixed batch per GPU). value = decode GB/s of the
+    step's decode part; the prefill part is reported as TFLOP/s of visible
+    (unmasked) query-key pairs."""
+    rank, world, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lir = importlib.import_module(PKG)
+    lir.build.build()
+    fi = importlib.import_module(PKG + ".flashinfer_api")
+    wl, geom, n_dec, lo, hi, layers, wname = _workload(args)
+    pre = wl.config3_prefill(seed=rank, device=dev)
+    dec = wl.make_decode_problem(geom, n_dec, lo, hi, seed=100 + rank, device=dev, num_layers=1,
+                                 append=False)
+    qo, kvp, kvi, last = pre.device_tables(dev)
+    dindptr, dindices, dlast = dec.device_tables(dev)
+    ws_p = torch.empty(128 << 20, dtype=torch.uint8, device=dev)
+    ws_d = torch.empty(128 << 20, dtype=torch.uint8, device=dev)
+    pw = fi.BatchPrefillWithPagedKVCacheWrapper(ws_p, "HND")
+    dw = fi.BatchDecodeWithPagedKVCacheWrapper(ws_d, "HND")
+    q_pre, q_dec = pre.q, dec.q
+    out_pre, out_dec = torch.empty_like(q_pre), torch.empty_like(q_dec)
+    flops = pre.flops(causal=True)
+    dbytes = dec.decode_bytes_per_layer()
+    stream = torch.cuda.current_stream()
+    ev = []
+
+    def step(record):
+        pw.plan(qo, kvp, kvi, last, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim, 16,
+                causal=True, q_data_type=q_pre.dtype, total_qo=q_pre.shape[0])
+        dw.plan(dindptr, dindices, dlast, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim,
+                16, q_data_type=q_dec.dtype)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
+        if record:
+            e[0].record(stream)
+        pw.run(q_pre, pre.pool[0], out=out_pre)
+        if record:
+            e[1].record(stream)
+        dw.run(q_dec, dec.pool[0], out=out_dec)
+        if record:
+            e[2].record(stream)
+            ev.append(e)
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    lir._lib.check_device("bench cfg3 warm-up")
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step(True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop()
+    ms = _max_over_ranks(t0.elapsed_time(t1), world)
+    pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    lir._lib.check_device("bench cfg3")
+    total_dbytes = _sum_over_ranks(float(dbytes) * args.steps, world)
+    value = total_dbytes / (ms * 1e-3) / 1e9
+    peak_bw, bw_kind = _peaks()
+    with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+        peak_tf = float(json.load(f)["bf16_tflops"])
+    pre_tf = flops / (pre_ms * 1e-3) / 1e12
+    dec_gbs = dbytes / (dec_ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) q/K/V, random page permutation",
+            "config": {"workload": wname, "layers": 1, "num_qo_heads": geom.num_qo_heads,
+                       "num_kv_heads": geom.num_kv_heads, "head_dim": geom.head_dim,
+                       "page_size": 16, "prefill": "16 chunks x 512 rows, prefix U[0,2048]",
+                       "decode_rows": n_dec, "context": f"U[{lo},{hi}]",
+                       "parallelism": f"request-sharded x{world}, no collective",
+                       "l2": "decode KV 1.1 GB per step exceeds L2"},
+            "roofline": {"bound": "hbm", "achieved": round(dec_gbs, 1), "peak": peak_bw,
+                         "unit": "GB/s", "frac": round(dec_gbs / peak_bw, 4),
+                         "peak_kind": bw_kind, "kernel": "decode_kernel",
+                         "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_ms, 5),
+                         "traffic": None},
+            "prefill": {"tflops": round(pre_tf, 1), "gflop_per_launch": round(flops / 1e9, 2),
+                        "avg_launch_ms": round(pre_ms, 5),
+                        "roofline": {"bound": "tensor", "achieved": round(pre_tf, 1),
+                                     "peak": peak_tf, "unit": "TFLOP/s",
+                                     "frac": round(pre_tf / peak_tf, 4),
+                                     "peak_kind": "measured (cuBLAS bf16 burst)",
+                                     "kernel": "prefill_kernel"}},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------- CPU side
 def cpu_baseline(prob_lengths: np.ndarray, geom, layers: int, budget_s: float = 15.0,
                  sample: int = 16) -> dict:
@@ -381,13 +495,15 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg5"], default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg3":
+        run_mixed(args)
     else:
         run_ours(args)
 

@@ -9,26 +9,69 @@
 // Work item = (request, kv head, query tile). The g query heads that share a
 // kv head are packed into the 128 rows of one tcgen05 tile (row = query * g +
 // head), so every K/V tile loaded serves the whole GQA group. Per CTA:
-//   * warp 4  — TMA producer: the Q tile once (3-D map over [tokens, heads,
+//   * warp 8  — TMA producer: the Q tile once (3-D map over [tokens, heads,
 //     dim], 128-byte swizzle), then K and V tiles of 8 pages (128 keys) into
 //     separate rings, each page one box per 64-column panel.
-//   * warp 5  — tcgen05 issuer (one thread): S_j = Q K_j^T into one of two
+//   * warp 9  — tcgen05 issuer (one thread): S_j = Q K_j^T into one of two
 //     TMEM S buffers, O += P_j V_j into a TMEM accumulator (fp32), completion
 //     reported through tcgen05.commit on mbarriers.
-//   * warps 0-3 — softmax / epilogue warpgroup, thread = row = TMEM lane:
-//     loads its S row, applies the causal / length mask and an online softmax
-//     in base 2 with lazy O rescaling (only when the running max grows by more
-//     than 2^8), writes P (bf16 / fp16) into a 128B-swizzled shared tile for
-//     the PV MMA, and finally normalises O and stores it.
+//   * warps 0-7 — softmax / epilogue, two threads per tile row (= TMEM lane),
+//     each on half of the keys: causal / length mask, online softmax in base
+//     2 with lazy O rescaling (only when the running max grows by more than
+//     2^8), P (bf16 / fp16) into one of two 128B-swizzled shared tiles for the
+//     PV MMA; finally O is normalised and stored.
 #pragma once
 
 #include "pa_common.cuh"
 
 namespace pa {
 
+// Share of the softmax exponentials evaluated on the FMA pipe instead of the
+// MUFU unit (column c uses the polynomial when c % 8 < kPfPolyOf8).
+#ifndef PA_PF_POLY_OF8
+#define PA_PF_POLY_OF8 0
+#endif
+constexpr int kPfPolyOf8 = PA_PF_POLY_OF8;
+
+// 2^x evaluated with FMA / integer instructions: x = n + f, n = round(x),
+// f in [-0.5, 0.5]; 2^f from a cubic fitted to 2^f on that interval
+// (weighted least squares, max relative error 7.5e-5), then n is added to
+// the exponent field. x below -126 (including -inf) returns 0.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float t = xc + 12582912.0f;  // 1.5 * 2^23: the low mantissa bits hold round(xc)
+  const float n = t - 12582912.0f;
+  const float f = xc - n;
+  const float p = fmaf(fmaf(fmaf(0.05517605f, f, 0.24261150f), f, 0.69326019f), f, 0.99992806f);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(p) + (ni << 23));
+  return x < -126.0f ? 0.0f : r;
+}
+
+// Two non-negative fp32 values -> packed 16-bit pair (lo in the low half).
+// bf16: round to nearest (ties away from zero) with integer ops, keeping the
+// conversion off the MUFU/XU pipe; fp16: the hardware conversion.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_p(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack_p<__nv_bfloat16>(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
+  return __byte_perm(a, b, 0x7632);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_p<__half>(float lo, float hi) {
+  return pack2<__half>(lo, hi);
+}
+
 constexpr int kPfRows = 128;  // query rows per tile (MMA M)
 constexpr int kPfKeys = 128;  // keys per K/V tile (MMA N of S, K of PV): 8 pages
-constexpr int kPfThreads = 192;
+// Warps 0-7: softmax / epilogue, two threads per tile row (warps w and w+4
+// share TMEM lanes 32*(w%4).., each takes half of the keys and of O's
+// columns); warp 8: TMA producer; warp 9: tcgen05 issuer.
+constexpr int kPfSoftmaxThreads = 256;
+constexpr int kPfProducerWarp = 8;
+constexpr int kPfMmaWarp = 9;
+constexpr int kPfThreads = 320;
 constexpr float kPfRescaleLog2 = 8.0f;
 
 struct PrefillPlanHeader {
@@ -67,16 +110,23 @@ struct PfCfg {
   static constexpr int kStages = D == 128 ? 2 : 4;
   static constexpr int kQBytes = kPfRows * D * 2;
   static constexpr int kTileBytes = kPfKeys * D * 2;  // one K or V tile
-  static constexpr int kPBytes = kPfRows * kPfKeys * 2;
+  static constexpr int kPBytes = kPfRows * kPfKeys * 2;  // one P buffer (two are kept)
   static constexpr int kPanelBytes = kPfRows * 128;    // 128 rows of 128 bytes
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffP = kOffV + kStages * kTileBytes;
-  static constexpr int kOffBar = kOffP + kPBytes;
-  // barriers: q_full, s_full[2], p_full, o_done, k_full/k_empty/v_full/v_empty[S]
-  static constexpr int kNumBars = 5 + 4 * kStages;
-  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+  static constexpr int kOffBar = kOffP + 2 * kPBytes;
+  // barriers: q_full, s_full[2], p_full, o_done, p_free[2], xbar,
+  // k_full/k_empty/v_full/v_empty[S]
+  static constexpr int kNumBars = 8 + 4 * kStages;
+  static constexpr int kOffXch = kOffBar + ((kNumBars * 8 + 16 + 15) / 16) * 16;
+  // row-max exchange between the two threads of a row, double-buffered by tile
+  static constexpr int kUsedBytes = kOffXch + 2 * kPfSoftmaxThreads * 4;
+  // 1 KiB of slack to align the base when it fits; otherwise the kernel
+  // requires (and checks) a 1024-byte aligned dynamic shared memory base.
+  static constexpr int kSlack = kUsedBytes + 1024 <= 232448 ? 1024 : 0;
+  static constexpr int kSmemBytes = kUsedBytes + kSlack;
   static constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O
 };
 
@@ -197,7 +247,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                    const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   using C = PfCfg<D>;
   constexpr int S = C::kStages;
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (C::kSlack == 0 && (smem_u32(smem_raw) & 1023) != 0) {
+    if (threadIdx.x == 0) set_status(PA_ERR_DEVICE_CHECK);
+    return;
+  }
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem + C::kOffQ;
   uint8_t* sK = smem + C::kOffK;
@@ -208,7 +262,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* s_full = bars + 1;  // [2]
   uint64_t* p_full = bars + 3;
   uint64_t* o_done = bars + 4;
-  uint64_t* k_full = bars + 5;
+  uint64_t* p_free = bars + 5;  // [2]: PV on that P buffer completed
+  uint64_t* xbar = bars + 7;    // row-max / row-sum exchange between the halves of a row
+  uint64_t* k_full = bars + 8;
   uint64_t* k_empty = k_full + S;
   uint64_t* v_full = k_empty + S;
   uint64_t* v_empty = v_full + S;
@@ -244,8 +300,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     mbar_init(q_full, 1);
     mbar_init(&s_full[0], 1);
     mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kPfSoftmaxThreads);
     mbar_init(o_done, 1);
+    mbar_init(&p_free[0], 1);
+    mbar_init(&p_free[1], 1);
+    mbar_init(xbar, kPfSoftmaxThreads);
     for (int s = 0; s < S; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -254,7 +313,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kPfMmaWarp) {
     tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
@@ -265,7 +324,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const uint32_t tS0 = tmem, tO = tmem + 256;
   bool failed = false;
 
-  if (warp == 4) {
+  if (warp == kPfProducerWarp) {
     // ------------------------------------------------------------ producer
     const int c1 = p.heads_inner ? h : 0, c2 = p.heads_inner ? 0 : h;
     if (lane == 0 && ntiles > 0) {
@@ -313,7 +372,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
     }
     if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
-  } else if (warp == 5) {
+  } else if (warp == kPfMmaWarp) {
     // ------------------------------------------------------------ tcgen05 issuer
     if (lane == 0 && ntiles > 0) {
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -350,12 +409,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
+          const uint32_t poff = (j & 1) * C::kPBytes + (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
           umma_f16(tO, umma_desc_sw128(p_base + poff, 16, 1024),
                    umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes, 1024),
                    idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&v_empty[st]);
+        umma_commit(&p_free[j & 1]);
         umma_commit(o_done);
         if (j + 2 < ntiles) issue_s(j + 2);
       }
@@ -363,14 +423,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int r = threadIdx.x;  // tile row == TMEM lane
+    constexpr int HK = kPfKeys / 2;  // keys of a tile this thread handles
+    constexpr int HD = D / 2;        // O columns this thread handles
+    const int half = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;  // tile row == TMEM lane
     const int qi = r / G, gi = r - qi * G;
     const bool row_ok = qi < QT && t0 + qi < qo_len;
     const int qpos = kv_len - qo_len + t0 + qi;
     const int lim = p.causal ? min(qpos + 1, kv_len) : kv_len;
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
     float m_used = -INFINITY, l = 0.f;
-    float s[kPfKeys];
+    float s[HK];
     for (int j = 0; j < ntiles; ++j) {
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
         failed = true;
@@ -378,74 +442,100 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kPfKeys / 32; ++c)
-        tmem_ld32(tS0 + lane_addr + (j & 1) * kPfKeys + c * 32, s + c * 32);
+      for (int c = 0; c < HK / 32; ++c)
+        tmem_ld32(tS0 + lane_addr + (j & 1) * kPfKeys + half * HK + c * 32, s + c * 32);
       tmem_wait_ld();
-      const int key0 = j * kPfKeys;
-      float mx = -INFINITY;
+      const int key0 = j * kPfKeys + half * HK;
+      // mask keys past this row's limit (only tiles that reach it need it)
+      if (!__all_sync(0xffffffffu, key0 + HK <= lim)) {
 #pragma unroll
-      for (int c = 0; c < kPfKeys; ++c) {
-        const float v = key0 + c < lim ? s[c] * p.scale_log2 : -INFINITY;
-        s[c] = v;
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < HK; ++c)
+          if (key0 + c >= lim) s[c] = -INFINITY;
       }
+      float mx8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx8[e] = s[e];
+#pragma unroll
+      for (int c = 8; c < HK; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      // combine with the other half of the row (exchange use j, bounded wait)
+      xch[(j & 1) * kPfSoftmaxThreads + threadIdx.x] = mx;
+      mbar_arrive(xbar);
+      if (!mbar_wait(xbar, j & 1)) {
+        failed = true;
+        break;
+      }
+      mx = fmaxf(mx, xch[(j & 1) * kPfSoftmaxThreads + (threadIdx.x ^ 128)]) * p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
       const bool need = m_new > m_used + kPfRescaleLog2;
-      if (j > 0) {
+      const float m_old = m_used;
+      if (need) m_used = m_new;
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      // P = 2^(s * scale - m) in registers before any wait on the tensor core
+      float l8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) l8[e] = 0.f;
+#pragma unroll
+      for (int c = 0; c < HK; ++c) {
+        const float x = fmaf(s[c], p.scale_log2, neg_m);
+        s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
+        l8[c & 7] += s[c];
+      }
+      const float lt = ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+      // Rows whose max moved rescale their half of O (after PV_{j-1}).
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
         if (!mbar_wait(o_done, (j - 1) & 1)) {
           failed = true;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-          // rescale the rows whose running max moved (O = O * 2^(m_old - m_new))
-          const float f = need ? ex2(m_used - m_new) : 1.f;
-          float o[32];
+        const float f = need ? ex2(m_old - m_used) : 1.f;
+        float o[32];
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            tmem_ld32(tO + lane_addr + c * 32, o);
-            tmem_wait_ld();
+        for (int c = 0; c < HD / 32; ++c) {
+          tmem_ld32(tO + lane_addr + half * HD + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= f;
-            tmem_st32(tO + lane_addr + c * 32, o);
-          }
-          tmem_wait_st();
-          l *= f;
+          for (int e = 0; e < 32; ++e) o[e] *= f;
+          tmem_st32(tO + lane_addr + half * HD + c * 32, o);
         }
+        tmem_wait_st();
+        l *= f;
       }
-      if (need) m_used = m_new;
-      const float ms = m_used == -INFINITY ? 0.f : m_used;
-      // P row -> swizzled K-major tile: 16-byte chunk q holds keys 8q..8q+7
+      l += lt;
+      // P buffer j&1 is free once PV_{j-2} completed.
+      if (j >= 2 && !mbar_wait(&p_free[j & 1], ((j >> 1) - 1) & 1)) {
+        failed = true;
+        break;
+      }
+      // this half's 64 keys = panel `half` of the K-major P tile
+      uint8_t* pbuf = sP + (j & 1) * C::kPBytes + half * C::kPanelBytes;
 #pragma unroll
-      for (int q = 0; q < kPfKeys / 8; ++q) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = ex2(s[q * 8 + e] - ms);
-          l += pv[e];
-        }
+      for (int q = 0; q < HK / 8; ++q) {
         uint4 w;
-        w.x = pack2<T>(pv[0], pv[1]);
-        w.y = pack2<T>(pv[2], pv[3]);
-        w.z = pack2<T>(pv[4], pv[5]);
-        w.w = pack2<T>(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(sP + (q >> 3) * C::kPanelBytes + sw128(r, q & 7)) = w;
+        w.x = pack_p<T>(s[q * 8 + 0], s[q * 8 + 1]);
+        w.y = pack_p<T>(s[q * 8 + 2], s[q * 8 + 3]);
+        w.z = pack_p<T>(s[q * 8 + 4], s[q * 8 + 5]);
+        w.w = pack_p<T>(s[q * 8 + 6], s[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(pbuf + sw128(r, q)) = w;
       }
       // The last tile may hold keys past kv_len (stale slots, pages never
       // loaded): zero those V rows so 0 * Inf cannot reach O.
-      if (j == ntiles - 1 && key0 + kPfKeys > kv_len) {
+      const int tile0 = j * kPfKeys;
+      if (j == ntiles - 1 && tile0 + kPfKeys > kv_len) {
         const int st = j % S;
         if (!mbar_wait(&v_full[st], (j / S) & 1)) {
           failed = true;
           break;
         }
-        if (key0 + r >= kv_len) {
+        if (tile0 + r >= kv_len) {
 #pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              *reinterpret_cast<uint4*>(sV + st * C::kTileBytes + pn * C::kPanelBytes + r * 128 +
-                                        c * 16) = make_uint4(0, 0, 0, 0);
+          for (int k = 0; k < 4 * C::kPanels; ++k) {
+            const int cidx = half * 4 * C::kPanels + k;
+            *reinterpret_cast<uint4*>(sV + st * C::kTileBytes + (cidx >> 3) * C::kPanelBytes +
+                                      r * 128 + (cidx & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
         }
       }
       fence_proxy_async();
@@ -456,18 +546,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (!failed && ntiles > 0) {
       if (!mbar_wait(o_done, (ntiles - 1) & 1)) failed = true;
     }
+    // the two halves' running sums share the same max: add them (exchange use ntiles)
+    if (!failed) {
+      xch[(ntiles & 1) * kPfSoftmaxThreads + threadIdx.x] = l;
+      mbar_arrive(xbar);
+      if (!mbar_wait(xbar, ntiles & 1)) failed = true;
+      else l += xch[(ntiles & 1) * kPfSoftmaxThreads + (threadIdx.x ^ 128)];
+    }
     if (failed) {
       set_status(PA_ERR_TIMEOUT);
     } else {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       T* orow = reinterpret_cast<T*>(p.out) +
-                (static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi) * D;
+                (static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi) * D + half * HD;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         float o[32];
         if (ntiles > 0) {
-          tmem_ld32(tO + lane_addr + c * 32, o);
+          tmem_ld32(tO + lane_addr + half * HD + c * 32, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -485,7 +582,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
         }
       }
-      if (row_ok && p.lse != nullptr)
+      if (row_ok && half == 0 && p.lse != nullptr)
         p.lse[static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi] =
             l > 0.f ? m_used + lg2(l) : -INFINITY;
     }
@@ -493,7 +590,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kPfMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }

@@ -377,7 +377,6 @@ class BatchPrefillWithPagedKVCacheWrapper:
         if head_dim_vo not in (None, head_dim_qk):
             raise NotImplementedError("head_dim_vo must equal head_dim_qk")
         device = self._ws.device
-        self._qo_indptr_host = qo_indptr.to("cpu") if qo_indptr.device.type == "cpu" else None
         self._qo_indptr = _i32_on(qo_indptr, device, "qo_indptr")
         self._indptr = _i32_on(paged_kv_indptr, device, "paged_kv_indptr")
         self._indices = _i32_on(paged_kv_indices, device, "paged_kv_indices")
@@ -386,11 +385,18 @@ class BatchPrefillWithPagedKVCacheWrapper:
         self._hq, self._hkv, self._d, self._p = num_qo_heads, num_kv_heads, head_dim_qk, page_size
         self._causal = bool(causal)
         self._sm_scale = sm_scale
-        # total_qo bounds the query rows; it is a shape, known on the host.
-        self._total_qo_bound = int(kwargs.get("max_total_qo", 0)) or None
         self._plan_total = None
         self._planned = True
         self._needs_device_plan = True
+        # The device plan needs the number of query rows (it sizes the work
+        # list). It is known here when qo_indptr lives on the host or the
+        # caller passes total_qo; otherwise the first run() plans, from
+        # q.size(0), without any device-to-host copy.
+        total = kwargs.get("total_qo")
+        if total is None and qo_indptr.device.type == "cpu":
+            total = int(qo_indptr[-1])
+        if total is not None:
+            self._device_plan(int(total))
 
     begin_forward = plan
 
