@@ -445,9 +445,9 @@ size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int3
   if (batch_size <= 0 || max_total_qo < 0 || num_kv_heads <= 0 || num_qo_heads <= 0 ||
       num_qo_heads % num_kv_heads || head_dim <= 0)
     return 0;
-  const int qt = prefill_qt(num_qo_heads / num_kv_heads);
-  if (qt == 0) return 0;
-  return prefill_ws_layout(prefill_max_items(batch_size, max_total_qo, num_kv_heads, qt)).total;
+  const int span = prefill_span(num_qo_heads / num_kv_heads);
+  if (span == 0) return 0;
+  return prefill_ws_layout(prefill_max_items(batch_size, max_total_qo, num_kv_heads, span)).total;
 }
 
 int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
@@ -461,16 +461,16 @@ int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
   if (batch_size <= 0 || total_qo < 0 || num_kv_indices < 0 || num_qo_heads <= 0 ||
       num_kv_heads <= 0 || num_qo_heads % num_kv_heads)
     return PA_ERR_INVALID_ARGUMENT;
-  const int qt = prefill_qt(num_qo_heads / num_kv_heads);
-  if (qt == 0) return PA_ERR_UNSUPPORTED;
+  const int span = prefill_span(num_qo_heads / num_kv_heads);
+  if (span == 0) return PA_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return PA_ERR_UNSUPPORTED;
   if (page_size != kPage) return PA_ERR_UNSUPPORTED;
   if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
-  const int64_t max_items = prefill_max_items(batch_size, total_qo, num_kv_heads, qt);
+  const int64_t max_items = prefill_max_items(batch_size, total_qo, num_kv_heads, span);
   if (prefill_ws_layout(max_items).total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
   prefill_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
       qo_indptr, kv_indptr, kv_last_page_len, batch_size, total_qo, num_kv_indices, num_qo_heads,
-      num_kv_heads, head_dim, page_size, qt, max_items, static_cast<uint8_t*>(workspace));
+      num_kv_heads, head_dim, page_size, span, max_items, static_cast<uint8_t*>(workspace));
   return launch_status();
 }
 
@@ -495,7 +495,7 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
   if (!aligned16(q) || !aligned16(out) || q_stride_n % 8 || q_stride_h % 8)
     return PA_ERR_INVALID_ARGUMENT;
   if (total_qo == 0) return PA_OK;
-  const int64_t max_items = prefill_max_items(batch_size, total_qo, hkv, qt);
+  const int64_t max_items = prefill_max_items(batch_size, total_qo, hkv, 2 * qt);
   const PrefillWsLayout L = prefill_ws_layout(max_items);
   if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
   CUtensorMap qm, km, vm;

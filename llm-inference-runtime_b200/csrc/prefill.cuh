@@ -6,20 +6,22 @@
 // causal masking (bottom-right aligned, FlashInfer's convention) query row i
 // of a request with qo_len rows sees key j iff j <= i + kv_len - qo_len.
 //
-// Work item = (request, kv head, query tile). The g query heads that share a
-// kv head are packed into the 128 rows of one tcgen05 tile (row = query * g +
-// head), so every K/V tile loaded serves the whole GQA group. Per CTA:
-//   * warp 8  — TMA producer: the Q tile once (3-D map over [tokens, heads,
+// Work item = (request, kv head, two query tiles). The g query heads that
+// share a kv head are packed into the 128 rows of a tcgen05 tile (row =
+// query * g + head), so every K/V tile loaded serves the whole GQA group, and
+// each CTA carries two such tiles so the tensor core always has one tile's
+// GEMMs to run while the other tile's softmax is in flight. Per CTA:
+//   * warp 8  — TMA producer: both Q tiles once (3-D map over [tokens, heads,
 //     dim], 128-byte swizzle), then K and V tiles of 8 pages (128 keys) into
 //     separate rings, each page one box per 64-column panel.
-//   * warp 9  — tcgen05 issuer (one thread): S_j = Q K_j^T into one of two
-//     TMEM S buffers, O += P_j V_j into a TMEM accumulator (fp32), completion
-//     reported through tcgen05.commit on mbarriers.
-//   * warps 0-7 — softmax / epilogue, two threads per tile row (= TMEM lane),
-//     each on half of the keys: causal / length mask, online softmax in base
-//     2 with lazy O rescaling (only when the running max grows by more than
-//     2^8), P (bf16 / fp16) into one of two 128B-swizzled shared tiles for the
-//     PV MMA; finally O is normalised and stored.
+//   * warp 9  — tcgen05 issuer (one thread), per K/V tile j and Q tile t:
+//     S_t = Q_t K_j^T (fp32, TMEM), then O_t += P_t V_j with P_t read from
+//     TMEM (bf16 / fp16 written over S_t's columns) and V_j from shared
+//     memory; completion reported through tcgen05.commit on mbarriers.
+//   * warps 0-3 / 4-7 — softmax + epilogue of Q tile 0 / 1, one thread per
+//     row (= TMEM lane): causal / length mask, online softmax in base 2 with
+//     lazy O rescaling (only when a row's max grows by more than 2^8), P back
+//     into TMEM; finally O is normalised and stored.
 #pragma once
 
 #include "pa_common.cuh"
@@ -65,9 +67,8 @@ __device__ __forceinline__ uint32_t pack_p<__half>(float lo, float hi) {
 
 constexpr int kPfRows = 128;  // query rows per tile (MMA M)
 constexpr int kPfKeys = 128;  // keys per K/V tile (MMA N of S, K of PV): 8 pages
-// Warps 0-7: softmax / epilogue, two threads per tile row (warps w and w+4
-// share TMEM lanes 32*(w%4).., each takes half of the keys and of O's
-// columns); warp 8: TMA producer; warp 9: tcgen05 issuer.
+// Warps 0-3 / 4-7: softmax + epilogue of Q tile 0 / 1; warp 8: TMA producer;
+// warp 9: tcgen05 issuer.
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
@@ -108,26 +109,18 @@ template <int D>
 struct PfCfg {
   static constexpr int kPanels = D / 64;
   static constexpr int kStages = D == 128 ? 2 : 4;
-  static constexpr int kQBytes = kPfRows * D * 2;
-  static constexpr int kTileBytes = kPfKeys * D * 2;  // one K or V tile
-  static constexpr int kPBytes = kPfRows * kPfKeys * 2;  // one P buffer (two are kept)
+  static constexpr int kQBytes = kPfRows * D * 2;      // one Q tile (two are kept)
+  static constexpr int kTileBytes = kPfKeys * D * 2;   // one K or V tile
   static constexpr int kPanelBytes = kPfRows * 128;    // 128 rows of 128 bytes
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kOffQ + kQBytes;
+  static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  static constexpr int kOffP = kOffV + kStages * kTileBytes;
-  static constexpr int kOffBar = kOffP + 2 * kPBytes;
-  // barriers: q_full, s_full[2], p_full, o_done, p_free[2], xbar,
-  // k_full/k_empty/v_full/v_empty[S]
-  static constexpr int kNumBars = 8 + 4 * kStages;
-  static constexpr int kOffXch = kOffBar + ((kNumBars * 8 + 16 + 15) / 16) * 16;
-  // row-max exchange between the two threads of a row, double-buffered by tile
-  static constexpr int kUsedBytes = kOffXch + 2 * kPfSoftmaxThreads * 4;
-  // 1 KiB of slack to align the base when it fits; otherwise the kernel
-  // requires (and checks) a 1024-byte aligned dynamic shared memory base.
-  static constexpr int kSlack = kUsedBytes + 1024 <= 232448 ? 1024 : 0;
-  static constexpr int kSmemBytes = kUsedBytes + kSlack;
-  static constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O
+  static constexpr int kOffBar = kOffV + kStages * kTileBytes;
+  // barriers: q_full, s_full[2], p_full[2], o_done[2], k_full/k_empty/v_full/v_empty[S]
+  static constexpr int kNumBars = 7 + 4 * kStages;
+  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+  // TMEM columns: S0 | S1 | O0 | O1 (P_t is written over the first half of S_t)
+  static constexpr uint32_t kTmemCols = 512;
 };
 
 struct PrefillParams {
@@ -241,30 +234,25 @@ __global__ void prefill_plan_kernel(const int32_t* __restrict__ qo_indptr,
 }
 
 // ---------------------------------------------------------------------- run
+// 10 warps share four 16 Ki-register sub-partitions (3/3/2/2 warps), which
+// caps the kernel at 168 registers per thread.
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
   using C = PfCfg<D>;
   constexpr int S = C::kStages;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  if (C::kSlack == 0 && (smem_u32(smem_raw) & 1023) != 0) {
-    if (threadIdx.x == 0) set_status(PA_ERR_DEVICE_CHECK);
-    return;
-  }
+  extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem + C::kOffQ;
   uint8_t* sK = smem + C::kOffK;
   uint8_t* sV = smem + C::kOffV;
-  uint8_t* sP = smem + C::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* s_full = bars + 1;  // [2]
-  uint64_t* p_full = bars + 3;
-  uint64_t* o_done = bars + 4;
-  uint64_t* p_free = bars + 5;  // [2]: PV on that P buffer completed
-  uint64_t* xbar = bars + 7;    // row-max / row-sum exchange between the halves of a row
-  uint64_t* k_full = bars + 8;
+  uint64_t* s_full = bars + 1;  // [2] per Q tile
+  uint64_t* p_full = bars + 3;  // [2]
+  uint64_t* o_done = bars + 5;  // [2]
+  uint64_t* k_full = bars + 7;
   uint64_t* k_empty = k_full + S;
   uint64_t* v_full = k_empty + S;
   uint64_t* v_empty = v_full + S;
@@ -274,7 +262,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const PrefillPlanHeader* hdr = p.hdr;
   if (hdr->magic != kPrefillMagic || hdr->batch_size != p.batch_size ||
       hdr->num_kv_heads != p.num_kv_heads || hdr->num_qo_heads != p.num_qo_heads ||
-      hdr->head_dim != D || hdr->queries_per_tile != p.qt) {
+      hdr->head_dim != D || hdr->queries_per_tile != 2 * p.qt) {
     if (blockIdx.x == 0 && threadIdx.x == 0) set_status(PA_ERR_NOT_PLANNED);
     return;
   }
@@ -288,8 +276,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int page0 = __ldg(p.kv_indptr + b);
   const int npages = __ldg(p.kv_indptr + b + 1) - page0;
   const int kv_len = npages > 0 ? (npages - 1) * kPage + __ldg(p.kv_last_page_len + b) : 0;
-  // keys this tile can see: up to the last query's position (causal) or all
-  const int q_hi = min(t0 + QT, qo_len);
+  // keys this item can see: up to its last query's position (causal) or all
+  const int q_hi = min(t0 + 2 * QT, qo_len);
   const int kv_end = p.causal ? min(kv_len, kv_len - qo_len + q_hi) : kv_len;
   const int ntiles = kv_end > 0 ? (kv_end + kPfKeys - 1) / kPfKeys : 0;
 
@@ -298,13 +286,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
     mbar_init(q_full, 1);
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(p_full, kPfSoftmaxThreads);
-    mbar_init(o_done, 1);
-    mbar_init(&p_free[0], 1);
-    mbar_init(&p_free[1], 1);
-    mbar_init(xbar, kPfSoftmaxThreads);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+      mbar_init(&o_done[t], 1);
+    }
     for (int s = 0; s < S; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -321,17 +307,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS0 = tmem, tO = tmem + 256;
   bool failed = false;
 
   if (warp == kPfProducerWarp) {
     // ------------------------------------------------------------ producer
     const int c1 = p.heads_inner ? h : 0, c2 = p.heads_inner ? 0 : h;
     if (lane == 0 && ntiles > 0) {
-      mbar_arrive_expect_tx(q_full, C::kQBytes);
+      mbar_arrive_expect_tx(q_full, 2 * C::kQBytes);
 #pragma unroll
-      for (int pn = 0; pn < C::kPanels; ++pn)
-        tma_load_3d(sQ + pn * C::kPanelBytes, &qmap, q_full, pn * 64, h * G, qo_start + t0);
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_load_3d(sQ + t * C::kQBytes + pn * C::kPanelBytes, &qmap, q_full, pn * 64, h * G,
+                      qo_start + t0 + t * QT);
     }
     for (int j = 0; j < ntiles && !failed; ++j) {
       const int st = j % S, use = j / S;
@@ -345,7 +333,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
       const uint32_t bytes = static_cast<uint32_t>(np) * C::kPanels * 2048;
-      // K tile j
       if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1)) failed = true;
       if (!failed) {
         if (lane == 0) mbar_arrive_expect_tx(&k_full[st], bytes);
@@ -357,7 +344,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         &k_full[st], pn * 64, c1, c2, page);
         }
       }
-      // V tile j
       if (!failed && use > 0 && !mbar_wait(&v_empty[st], (use - 1) & 1)) failed = true;
       if (!failed) {
         if (lane == 0) mbar_arrive_expect_tx(&v_full[st], bytes);
@@ -378,180 +364,176 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_s = umma_idesc_f16(ab, kPfRows, kPfKeys, 0);
       const uint32_t idesc_o = umma_idesc_f16(ab, kPfRows, D, 1);
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV),
-                     p_base = smem_u32(sP);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       if (!mbar_wait(q_full, 0)) failed = true;
-      auto issue_s = [&](int j) {
+      // S_t = Q_t K_j^T into TMEM columns [128 t, 128 t + 128)
+      auto issue_s = [&](int t, int j) {
         const int st = j % S;
-        if (!mbar_wait(&k_full[st], (j / S) & 1)) {
-          failed = true;
-          return;
+        if (t == 0) {
+          if (!mbar_wait(&k_full[st], (j / S) & 1)) {
+            failed = true;
+            return;
+          }
+          tc_fence_after();
         }
-        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
-          umma_f16(tS0 + (j & 1) * kPfKeys, umma_desc_sw128(q_base + off, 16, 1024),
+          umma_f16(tmem + t * kPfKeys,
+                   umma_desc_sw128(q_base + t * C::kQBytes + off, 16, 1024),
                    umma_desc_sw128(k_base + st * C::kTileBytes + off, 16, 1024), idesc_s,
                    kk > 0 ? 1u : 0u);
         }
-        umma_commit(&k_empty[st]);
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[t]);
+        if (t == 1) umma_commit(&k_empty[st]);
       };
-      if (!failed) issue_s(0);
-      if (!failed && ntiles > 1) issue_s(1);
+      if (!failed) issue_s(0, 0);
+      if (!failed) issue_s(1, 0);
       for (int j = 0; j < ntiles && !failed; ++j) {
-        const int st = j % S;
-        if (!mbar_wait(p_full, j & 1) || !mbar_wait(&v_full[st], (j / S) & 1)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-          const uint32_t poff = (j & 1) * C::kPBytes + (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
-          umma_f16(tO, umma_desc_sw128(p_base + poff, 16, 1024),
-                   umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes, 1024),
-                   idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(&v_empty[st]);
-        umma_commit(&p_free[j & 1]);
-        umma_commit(o_done);
-        if (j + 2 < ntiles) issue_s(j + 2);
-      }
-      if (failed) set_status(PA_ERR_TIMEOUT);
-    }
-  } else {
-    // ------------------------------------------------------------ softmax + epilogue
-    constexpr int HK = kPfKeys / 2;  // keys of a tile this thread handles
-    constexpr int HD = D / 2;        // O columns this thread handles
-    const int half = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;  // tile row == TMEM lane
-    const int qi = r / G, gi = r - qi * G;
-    const bool row_ok = qi < QT && t0 + qi < qo_len;
-    const int qpos = kv_len - qo_len + t0 + qi;
-    const int lim = p.causal ? min(qpos + 1, kv_len) : kv_len;
-    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    float* xch = reinterpret_cast<float*>(smem + C::kOffXch);
-    float m_used = -INFINITY, l = 0.f;
-    float s[HK];
-    for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
-        failed = true;
-        break;
-      }
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < HK / 32; ++c)
-        tmem_ld32(tS0 + lane_addr + (j & 1) * kPfKeys + half * HK + c * 32, s + c * 32);
-      tmem_wait_ld();
-      const int key0 = j * kPfKeys + half * HK;
-      // mask keys past this row's limit (only tiles that reach it need it)
-      if (!__all_sync(0xffffffffu, key0 + HK <= lim)) {
-#pragma unroll
-        for (int c = 0; c < HK; ++c)
-          if (key0 + c >= lim) s[c] = -INFINITY;
-      }
-      float mx8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = s[e];
-#pragma unroll
-      for (int c = 8; c < HK; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      // combine with the other half of the row (exchange use j, bounded wait)
-      xch[(j & 1) * kPfSoftmaxThreads + threadIdx.x] = mx;
-      mbar_arrive(xbar);
-      if (!mbar_wait(xbar, j & 1)) {
-        failed = true;
-        break;
-      }
-      mx = fmaxf(mx, xch[(j & 1) * kPfSoftmaxThreads + (threadIdx.x ^ 128)]) * p.scale_log2;
-      const float m_new = fmaxf(m_used, mx);
-      const bool need = m_new > m_used + kPfRescaleLog2;
-      const float m_old = m_used;
-      if (need) m_used = m_new;
-      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-      // P = 2^(s * scale - m) in registers before any wait on the tensor core
-      float l8[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) l8[e] = 0.f;
-#pragma unroll
-      for (int c = 0; c < HK; ++c) {
-        const float x = fmaf(s[c], p.scale_log2, neg_m);
-        s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
-        l8[c & 7] += s[c];
-      }
-      const float lt = ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-      // Rows whose max moved rescale their half of O (after PV_{j-1}).
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        if (!mbar_wait(o_done, (j - 1) & 1)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
-        const float f = need ? ex2(m_old - m_used) : 1.f;
-        float o[32];
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-          tmem_ld32(tO + lane_addr + half * HD + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] *= f;
-          tmem_st32(tO + lane_addr + half * HD + c * 32, o);
-        }
-        tmem_wait_st();
-        l *= f;
-      }
-      l += lt;
-      // P buffer j&1 is free once PV_{j-2} completed.
-      if (j >= 2 && !mbar_wait(&p_free[j & 1], ((j >> 1) - 1) & 1)) {
-        failed = true;
-        break;
-      }
-      // this half's 64 keys = panel `half` of the K-major P tile
-      uint8_t* pbuf = sP + (j & 1) * C::kPBytes + half * C::kPanelBytes;
-#pragma unroll
-      for (int q = 0; q < HK / 8; ++q) {
-        uint4 w;
-        w.x = pack_p<T>(s[q * 8 + 0], s[q * 8 + 1]);
-        w.y = pack_p<T>(s[q * 8 + 2], s[q * 8 + 3]);
-        w.z = pack_p<T>(s[q * 8 + 4], s[q * 8 + 5]);
-        w.w = pack_p<T>(s[q * 8 + 6], s[q * 8 + 7]);
-        *reinterpret_cast<uint4*>(pbuf + sw128(r, q)) = w;
-      }
-      // The last tile may hold keys past kv_len (stale slots, pages never
-      // loaded): zero those V rows so 0 * Inf cannot reach O.
-      const int tile0 = j * kPfKeys;
-      if (j == ntiles - 1 && tile0 + kPfKeys > kv_len) {
         const int st = j % S;
         if (!mbar_wait(&v_full[st], (j / S) & 1)) {
           failed = true;
           break;
         }
-        if (tile0 + r >= kv_len) {
-#pragma unroll
-          for (int k = 0; k < 4 * C::kPanels; ++k) {
-            const int cidx = half * 4 * C::kPanels + k;
-            *reinterpret_cast<uint4*>(sV + st * C::kTileBytes + (cidx >> 3) * C::kPanelBytes +
-                                      r * 128 + (cidx & 7) * 16) = make_uint4(0, 0, 0, 0);
+        for (int t = 0; t < 2 && !failed; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1)) {
+            failed = true;
+            break;
           }
+          tc_fence_after();
+          // O_t += P_t V_j; P_t: TMEM columns [128 t, 128 t + 64), 16 keys per 8 columns
+#pragma unroll
+          for (int kk = 0; kk < kPfKeys / 16; ++kk) {
+            const uint32_t a_tmem = tmem + t * kPfKeys + kk * 8;
+            const uint64_t bdesc =
+                umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes, 1024);
+            asm volatile(
+                "{\n"
+                "  .reg .pred p;\n"
+                "  setp.ne.b32 p, %4, 0;\n"
+                "  tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+                "}\n" ::"r"(tmem + 256 + t * D),
+                "r"(a_tmem), "l"(bdesc), "r"(idesc_o), "r"((j > 0 || kk > 0) ? 1u : 0u)
+                : "memory");
+          }
+          umma_commit(&o_done[t]);
+          if (t == 1) umma_commit(&v_empty[st]);
+          // the next S_t overwrites P_t only after this PV (same issuing thread, in order)
+          if (j + 1 < ntiles) issue_s(t, j + 1);
         }
       }
-      fence_proxy_async();
+      if (failed) set_status(PA_ERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;                 // Q tile
+    const int r = (warp & 3) * 32 + lane;    // tile row == TMEM lane
+    const int qi = t * QT + r / G, gi = r % G;
+    const bool row_ok = r / G < QT && t0 + qi < qo_len;
+    const int qpos = kv_len - qo_len + t0 + qi;
+    const int lim = p.causal ? min(qpos + 1, kv_len) : kv_len;
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + t * kPfKeys;
+    const uint32_t tO = tmem + lane_addr + 256 + t * D;
+    float m_used = -INFINITY, l = 0.f;
+    float s[64];
+    for (int j = 0; j < ntiles; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const int key0 = j * kPfKeys;
+      const bool masked = !__all_sync(0xffffffffu, key0 + kPfKeys <= lim);
+      // pass 1: row max, 64 columns at a time
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        tmem_ld32(tS + hf * 64, s);
+        tmem_ld32(tS + hf * 64 + 32, s + 32);
+        tmem_wait_ld();
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (key0 + hf * 64 + c >= lim) s[c] = -INFINITY;
+        }
+#pragma unroll
+        for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+      const float m_new = fmaxf(m_used, mx);
+      const bool need = m_new > m_used + kPfRescaleLog2;
+      const float m_old = m_used;
+      if (need) m_used = m_new;
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      // Rows whose max moved rescale O_t (after PV_t of the previous tile).
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (!mbar_wait(&o_done[t], (j - 1) & 1)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const float f = need ? ex2(m_old - m_used) : 1.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          tmem_ld32(tO + c * 32, s);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[e] *= f;
+          tmem_st32(tO + c * 32, s);
+        }
+        l *= f;
+      }
+      // pass 2: P = 2^(s * scale - m) as 16-bit pairs over the first 64
+      // columns of S_t (each half lands on columns already read)
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        tmem_ld32(tS + hf * 64, s);
+        tmem_ld32(tS + hf * 64 + 32, s + 32);
+        tmem_wait_ld();
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (key0 + hf * 64 + c >= lim) s[c] = -INFINITY;
+        }
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float x = fmaf(s[c], p.scale_log2, neg_m);
+          s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
+          l4[c & 3] += s[c];
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(pack_p<T>(s[2 * e], s[2 * e + 1]));
+        tmem_st32(tS + hf * 32, s);
+      }
+      tmem_wait_st();
+      l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      // The last tile may hold keys past kv_len (stale slots, pages never
+      // loaded): tile 0's warpgroup zeroes those V rows before its PV, which
+      // precedes tile 1's PV on the tensor pipe.
+      if (t == 0 && j == ntiles - 1 && key0 + kPfKeys > kv_len) {
+        const int st = j % S;
+        if (!mbar_wait(&v_full[st], (j / S) & 1)) {
+          failed = true;
+          break;
+        }
+        if (key0 + r >= kv_len) {
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(sV + st * C::kTileBytes + pn * C::kPanelBytes + r * 128 +
+                                        c * 16) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
+      }
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[t]);
     }
-    // ---- epilogue: O / l -> out, LSE
+    // ---- epilogue: O_t / l -> out, LSE
     if (!failed && ntiles > 0) {
-      if (!mbar_wait(o_done, (ntiles - 1) & 1)) failed = true;
-    }
-    // the two halves' running sums share the same max: add them (exchange use ntiles)
-    if (!failed) {
-      xch[(ntiles & 1) * kPfSoftmaxThreads + threadIdx.x] = l;
-      mbar_arrive(xbar);
-      if (!mbar_wait(xbar, ntiles & 1)) failed = true;
-      else l += xch[(ntiles & 1) * kPfSoftmaxThreads + (threadIdx.x ^ 128)];
+      if (!mbar_wait(&o_done[t], (ntiles - 1) & 1)) failed = true;
     }
     if (failed) {
       set_status(PA_ERR_TIMEOUT);
@@ -559,12 +541,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       T* orow = reinterpret_cast<T*>(p.out) +
-                (static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi) * D + half * HD;
+                (static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi) * D;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         float o[32];
         if (ntiles > 0) {
-          tmem_ld32(tO + lane_addr + half * HD + c * 32, o);
+          tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -582,7 +564,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           }
         }
       }
-      if (row_ok && half == 0 && p.lse != nullptr)
+      if (row_ok && p.lse != nullptr)
         p.lse[static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi] =
             l > 0.f ? m_used + lg2(l) : -INFINITY;
     }
@@ -597,9 +579,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
+// Queries per 128-row tile for a GQA group size (rows = queries * group).
 inline int prefill_qt(int group) {
   return (group == 1 || group == 2 || group == 4 || group == 8 || group == 16) ? kPfRows / group
                                                                                 : 0;
 }
+
+// Queries per work item (two tiles).
+inline int prefill_span(int group) { return 2 * prefill_qt(group); }
 
 }  // namespace pa
