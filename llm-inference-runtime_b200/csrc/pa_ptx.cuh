@@ -296,6 +296,16 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_type, int m, int n,
          (static_cast<uint32_t>(m >> 4) << 24);        // M / 16
 }
 
+// Warpgroup register reallocation (all four warps of a warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

@@ -67,12 +67,19 @@ __device__ __forceinline__ uint32_t pack_p<__half>(float lo, float hi) {
 
 constexpr int kPfRows = 128;  // query rows per tile (MMA M)
 constexpr int kPfKeys = 128;  // keys per K/V tile (MMA N of S, K of PV): 8 pages
-// Warps 0-3 / 4-7: softmax + epilogue of Q tile 0 / 1; warp 8: TMA producer;
-// warp 9: tcgen05 issuer.
+// Warpgroups 0 / 1 (warps 0-3 / 4-7): softmax + epilogue of Q tile 0 / 1.
+// Warpgroup 2: warp 8 TMA producer, warp 9 tcgen05 issuer, warps 10-11 idle.
+// Launched at 168 registers per thread (384 x 168 = 64512 of 65536); after
+// setup warpgroup 2 drops to 56 and warpgroups 0-1 rise to 224:
+// 2 x 128 x 224 + 128 x 56 = 64512, exactly the launch total.
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
-constexpr int kPfThreads = 320;
+constexpr int kPfThreads = 384;
+constexpr uint32_t kPfRegsSoftmax = 224;
+constexpr uint32_t kPfRegsOther = 56;
+static_assert(2 * 128 * kPfRegsSoftmax + 128 * kPfRegsOther == kPfThreads * 168,
+              "register split must equal the launch allocation");
 constexpr float kPfRescaleLog2 = 8.0f;
 
 struct PrefillPlanHeader {
@@ -234,8 +241,6 @@ __global__ void prefill_plan_kernel(const int32_t* __restrict__ qo_indptr,
 }
 
 // ---------------------------------------------------------------------- run
-// 10 warps share four 16 Ki-register sub-partitions (3/3/2/2 warps), which
-// caps the kernel at 168 registers per thread.
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -308,8 +313,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
-
   if (warp == kPfProducerWarp) {
+    regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ producer
     const int c1 = p.heads_inner ? h : 0, c2 = p.heads_inner ? 0 : h;
     if (lane == 0 && ntiles > 0) {
@@ -359,6 +364,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
   } else if (warp == kPfMmaWarp) {
+    regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ tcgen05 issuer
     if (lane == 0 && ntiles > 0) {
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
@@ -424,7 +430,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       if (failed) set_status(PA_ERR_TIMEOUT);
     }
+  } else if (warp >= 10) {
+    regs_dec<kPfRegsOther>();
   } else {
+    regs_inc<kPfRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;                 // Q tile
     const int r = (warp & 3) * 32 + lane;    // tile row == TMEM lane
@@ -436,36 +445,44 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t tS = tmem + lane_addr + t * kPfKeys;
     const uint32_t tO = tmem + lane_addr + 256 + t * D;
     float m_used = -INFINITY, l = 0.f;
-    float s[64];
+    float s[kPfKeys];
     for (int j = 0; j < ntiles; ++j) {
       if (!mbar_wait(&s_full[t], j & 1)) {
         failed = true;
         break;
       }
       tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kPfKeys / 32; ++c) tmem_ld32(tS + c * 32, s + c * 32);
+      tmem_wait_ld();
       const int key0 = j * kPfKeys;
-      const bool masked = !__all_sync(0xffffffffu, key0 + kPfKeys <= lim);
-      // pass 1: row max, 64 columns at a time
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (!__all_sync(0xffffffffu, key0 + kPfKeys <= lim)) {
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        tmem_ld32(tS + hf * 64, s);
-        tmem_ld32(tS + hf * 64 + 32, s + 32);
-        tmem_wait_ld();
-        if (masked) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (key0 + hf * 64 + c >= lim) s[c] = -INFINITY;
-        }
-#pragma unroll
-        for (int c = 0; c < 64; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+        for (int c = 0; c < kPfKeys; ++c)
+          if (key0 + c >= lim) s[c] = -INFINITY;
       }
+      float mx4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mx4[e] = s[e];
+#pragma unroll
+      for (int c = 4; c < kPfKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
       const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       const float m_new = fmaxf(m_used, mx);
       const bool need = m_new > m_used + kPfRescaleLog2;
       const float m_old = m_used;
       if (need) m_used = m_new;
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < kPfKeys; ++c) {
+        const float x = fmaf(s[c], p.scale_log2, neg_m);
+        s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
+        l4[c & 3] += s[c];
+      }
+      // P_t as 16-bit pairs, packed in place over s[0..63]
+#pragma unroll
+      for (int e = 0; e < kPfKeys / 2; ++e)
+        s[e] = __uint_as_float(pack_p<T>(s[2 * e], s[2 * e + 1]));
       // Rows whose max moved rescale O_t (after PV_t of the previous tile).
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         if (!mbar_wait(&o_done[t], (j - 1) & 1)) {
@@ -474,41 +491,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         tc_fence_after();
         const float f = need ? ex2(m_old - m_used) : 1.f;
+        float o[32];
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          tmem_ld32(tO + c * 32, s);
+          tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) s[e] *= f;
-          tmem_st32(tO + c * 32, s);
+          for (int e = 0; e < 32; ++e) o[e] *= f;
+          tmem_st32(tO + c * 32, o);
         }
         l *= f;
       }
-      // pass 2: P = 2^(s * scale - m) as 16-bit pairs over the first 64
-      // columns of S_t (each half lands on columns already read)
-      float l4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        tmem_ld32(tS + hf * 64, s);
-        tmem_ld32(tS + hf * 64 + 32, s + 32);
-        tmem_wait_ld();
-        if (masked) {
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (key0 + hf * 64 + c >= lim) s[c] = -INFINITY;
-        }
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float x = fmaf(s[c], p.scale_log2, neg_m);
-          s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
-          l4[c & 3] += s[c];
-        }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(pack_p<T>(s[2 * e], s[2 * e + 1]));
-        tmem_st32(tS + hf * 32, s);
-      }
-      tmem_wait_st();
       l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+      // P_t over the first 64 columns of S_t
+      tmem_st32(tS, s);
+      tmem_st32(tS + 32, s + 32);
+      tmem_wait_st();
       // The last tile may hold keys past kv_len (stale slots, pages never
       // loaded): tile 0's warpgroup zeroes those V rows before its PV, which
       // precedes tile 1's PV on the tensor pipe.
