@@ -57,8 +57,9 @@ template <typename T>
 __device__ __forceinline__ uint32_t pack_p(float lo, float hi);
 template <>
 __device__ __forceinline__ uint32_t pack_p<__nv_bfloat16>(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
-  return __byte_perm(a, b, 0x7632);
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 template <>
 __device__ __forceinline__ uint32_t pack_p<__half>(float lo, float hi) {
@@ -76,10 +77,18 @@ constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
 constexpr int kPfThreads = 384;
-constexpr uint32_t kPfRegsSoftmax = 224;
-constexpr uint32_t kPfRegsOther = 56;
-static_assert(2 * 128 * kPfRegsSoftmax + 128 * kPfRegsOther == kPfThreads * 168,
-              "register split must equal the launch allocation");
+#ifndef PA_PF_REGS_SOFTMAX
+#define PA_PF_REGS_SOFTMAX 224
+#endif
+#ifndef PA_PF_REGS_OTHER
+#define PA_PF_REGS_OTHER 56
+#endif
+constexpr uint32_t kPfRegsSoftmax = PA_PF_REGS_SOFTMAX;
+constexpr uint32_t kPfRegsOther = PA_PF_REGS_OTHER;
+static_assert(2 * 128 * kPfRegsSoftmax + 128 * kPfRegsOther <= kPfThreads * 168,
+              "register split must fit the launch allocation");
+static_assert(kPfRegsSoftmax % 8 == 0 && kPfRegsOther % 8 == 0 && kPfRegsOther >= 24,
+              "setmaxnreg counts are multiples of 8 in [24, 256]");
 constexpr float kPfRescaleLog2 = 8.0f;
 
 struct PrefillPlanHeader {
@@ -293,7 +302,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     mbar_init(q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 128);
+      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
       mbar_init(&o_done[t], 1);
     }
     for (int s = 0; s < S; ++s) {
@@ -338,7 +347,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
       }
       const uint32_t bytes = static_cast<uint32_t>(np) * C::kPanels * 2048;
-      if (use > 0 && !mbar_wait(&k_empty[st], (use - 1) & 1)) failed = true;
+      if (use > 0 && !mbar_wait_warp(&k_empty[st], (use - 1) & 1)) failed = true;
       if (!failed) {
         if (lane == 0) mbar_arrive_expect_tx(&k_full[st], bytes);
         __syncwarp();
@@ -349,7 +358,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         &k_full[st], pn * 64, c1, c2, page);
         }
       }
-      if (!failed && use > 0 && !mbar_wait(&v_empty[st], (use - 1) & 1)) failed = true;
+      if (!failed && use > 0 && !mbar_wait_warp(&v_empty[st], (use - 1) & 1)) failed = true;
       if (!failed) {
         if (lane == 0) mbar_arrive_expect_tx(&v_full[st], bytes);
         __syncwarp();
@@ -447,7 +456,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     float m_used = -INFINITY, l = 0.f;
     float s[kPfKeys];
     for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_full[t], j & 1)) {
+      if (!mbar_wait_warp(&s_full[t], j & 1)) {
         failed = true;
         break;
       }
@@ -473,19 +482,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (need) m_used = m_new;
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
       float l4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P_t as 16-bit pairs, packed in place over s[0..63] and stored over the
+      // first 64 columns of S_t in 32-key chunks as they are produced
 #pragma unroll
-      for (int c = 0; c < kPfKeys; ++c) {
-        const float x = fmaf(s[c], p.scale_log2, neg_m);
-        s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
-        l4[c & 3] += s[c];
+      for (int ch = 0; ch < kPfKeys / 32; ++ch) {
+#pragma unroll
+        for (int c = 32 * ch; c < 32 * ch + 32; ++c) {
+          const float x = fmaf(s[c], p.scale_log2, neg_m);
+          s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
+          l4[c & 3] += s[c];
+        }
+#pragma unroll
+        for (int e = 16 * ch; e < 16 * ch + 16; ++e)
+          s[e] = __uint_as_float(pack_p<T>(s[2 * e], s[2 * e + 1]));
+        tmem_st16(tS + 16 * ch, s + 16 * ch);
       }
-      // P_t as 16-bit pairs, packed in place over s[0..63]
-#pragma unroll
-      for (int e = 0; e < kPfKeys / 2; ++e)
-        s[e] = __uint_as_float(pack_p<T>(s[2 * e], s[2 * e + 1]));
       // Rows whose max moved rescale O_t (after PV_t of the previous tile).
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        if (!mbar_wait(&o_done[t], (j - 1) & 1)) {
+        if (!mbar_wait_warp(&o_done[t], (j - 1) & 1)) {
           failed = true;
           break;
         }
@@ -503,16 +517,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         l *= f;
       }
       l += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-      // P_t over the first 64 columns of S_t
-      tmem_st32(tS, s);
-      tmem_st32(tS + 32, s + 32);
       tmem_wait_st();
       // The last tile may hold keys past kv_len (stale slots, pages never
       // loaded): tile 0's warpgroup zeroes those V rows before its PV, which
       // precedes tile 1's PV on the tensor pipe.
       if (t == 0 && j == ntiles - 1 && key0 + kPfKeys > kv_len) {
         const int st = j % S;
-        if (!mbar_wait(&v_full[st], (j / S) & 1)) {
+        if (!mbar_wait_warp(&v_full[st], (j / S) & 1)) {
           failed = true;
           break;
         }
@@ -527,11 +538,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         fence_proxy_async();
       }
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // ---- epilogue: O_t / l -> out, LSE
     if (!failed && ntiles > 0) {
-      if (!mbar_wait(&o_done[t], (ntiles - 1) & 1)) failed = true;
+      if (!mbar_wait_warp(&o_done[t], (ntiles - 1) & 1)) failed = true;
     }
     if (failed) {
       set_status(PA_ERR_TIMEOUT);
