@@ -51,8 +51,8 @@ __device__ __forceinline__ float exp2_fma(float x) {
 }
 
 // Two non-negative fp32 values -> packed 16-bit pair (lo in the low half).
-// bf16: round to nearest (ties away from zero) with integer ops, keeping the
-// conversion off the MUFU/XU pipe; fp16: the hardware conversion.
+// Both types: the hardware round-to-nearest-even conversion, one instruction
+// per pair.
 template <typename T>
 __device__ __forceinline__ uint32_t pack_p(float lo, float hi);
 template <>
