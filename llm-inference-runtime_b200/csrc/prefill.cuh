@@ -69,13 +69,22 @@ __device__ __forceinline__ uint32_t pack_p<__half>(float lo, float hi) {
 constexpr int kPfRows = 128;  // query rows per tile (MMA M)
 constexpr int kPfKeys = 128;  // keys per K/V tile (MMA N of S, K of PV): 8 pages
 // Warpgroups 0 / 1 (warps 0-3 / 4-7): softmax + epilogue of Q tile 0 / 1.
-// Warpgroup 2: warp 8 TMA producer, warp 9 tcgen05 issuer, warps 10-11 idle.
+// Warpgroup 2: warp 8 TMA producer, warp 9 tcgen05 issuer, warp 10 relays
+// TMA completions to the issuer, warp 11 idle.
 // Launched at 168 registers per thread (384 x 168 = 64512 of 65536); after
 // setup warpgroup 2 drops to 56 and warpgroups 0-1 rise to 224:
 // 2 x 128 x 224 + 128 x 56 = 64512, exactly the launch total.
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
+constexpr int kPfRelayWarp = 10;
+// Named barriers (0 is __syncthreads): P_t written (softmax warpgroup t ->
+// issuer warp), K / V tile landed (relay warp -> issuer warp).
+constexpr int kPfBarP = 1;  // + t
+constexpr int kPfBarK = 3;
+constexpr int kPfBarV = 4;
+constexpr int kPfBarPThreads = 128 + 32;
+constexpr int kPfBarKVThreads = 32 + 32;
 constexpr int kPfThreads = 384;
 #ifndef PA_PF_REGS_SOFTMAX
 #define PA_PF_REGS_SOFTMAX 224
@@ -132,8 +141,8 @@ struct PfCfg {
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-  // barriers: q_full, s_full[2], p_full[2], o_done[2], k_full/k_empty/v_full/v_empty[S]
-  static constexpr int kNumBars = 7 + 4 * kStages;
+  // barriers: q_full, s_full[2], o_done[2], mma_done, k_full/k_empty/v_full/v_empty[S]
+  static constexpr int kNumBars = 6 + 4 * kStages;
   static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
   // TMEM columns: S0 | S1 | O0 | O1 (P_t is written over the first half of S_t)
   static constexpr uint32_t kTmemCols = 512;
@@ -264,9 +273,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* s_full = bars + 1;  // [2] per Q tile
-  uint64_t* p_full = bars + 3;  // [2]
-  uint64_t* o_done = bars + 5;  // [2]
-  uint64_t* k_full = bars + 7;
+  uint64_t* o_done = bars + 3;    // [2]
+  uint64_t* mma_done = bars + 5;  // every MMA of the item has completed
+  uint64_t* k_full = bars + 6;
   uint64_t* k_empty = k_full + S;
   uint64_t* v_full = k_empty + S;
   uint64_t* v_empty = v_full + S;
@@ -302,7 +311,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     mbar_init(q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
       mbar_init(&o_done[t], 1);
     }
     for (int s = 0; s < S; ++s) {
@@ -311,6 +319,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
+    mbar_init(mma_done, 1);
     fence_mbar_init();
   }
   if (warp == kPfMmaWarp) {
@@ -375,71 +384,80 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == kPfMmaWarp) {
     regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ tcgen05 issuer
-    if (lane == 0 && ntiles > 0) {
+    // The whole warp runs this loop (it takes part in the named barriers);
+    // lane 0 issues, as predicated instructions. The issuing thread touches
+    // no shared memory between MMAs: with only a couple of MMAs queued, a
+    // shared-memory wait on this thread would idle the tensor pipe. Its
+    // hand-offs are named barriers: P_t from softmax warpgroup t, K / V
+    // tiles from the relay warp.
+    const uint32_t issue = lane == 0 ? 1u : 0u;
+    if (ntiles > 0) {
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_s = umma_idesc_f16(ab, kPfRows, kPfKeys, 0);
       const uint32_t idesc_o = umma_idesc_f16(ab, kPfRows, D, 1);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-      if (!mbar_wait(q_full, 0)) failed = true;
+      if (!mbar_wait_warp(q_full, 0)) failed = true;
       // S_t = Q_t K_j^T into TMEM columns [128 t, 128 t + 128)
       auto issue_s = [&](int t, int j) {
         const int st = j % S;
         if (t == 0) {
-          if (!mbar_wait(&k_full[st], (j / S) & 1)) {
-            failed = true;
-            return;
-          }
+          named_bar_sync(kPfBarK, kPfBarKVThreads);
           tc_fence_after();
         }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
-          umma_f16(tmem + t * kPfKeys,
-                   umma_desc_sw128(q_base + t * C::kQBytes + off, 16, 1024),
-                   umma_desc_sw128(k_base + st * C::kTileBytes + off, 16, 1024), idesc_s,
-                   kk > 0 ? 1u : 0u);
+          umma_f16_if(issue, tmem + t * kPfKeys,
+                      umma_desc_sw128(q_base + t * C::kQBytes + off, 16, 1024),
+                      umma_desc_sw128(k_base + st * C::kTileBytes + off, 16, 1024), idesc_s,
+                      kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[t]);
-        if (t == 1) umma_commit(&k_empty[st]);
+        umma_commit_if(issue, &s_full[t]);
+        if (t == 1) umma_commit_if(issue, &k_empty[st]);
       };
-      if (!failed) issue_s(0, 0);
-      if (!failed) issue_s(1, 0);
-      for (int j = 0; j < ntiles && !failed; ++j) {
+      issue_s(0, 0);
+      issue_s(1, 0);
+      for (int j = 0; j < ntiles; ++j) {
         const int st = j % S;
-        if (!mbar_wait(&v_full[st], (j / S) & 1)) {
-          failed = true;
-          break;
-        }
-        for (int t = 0; t < 2 && !failed; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1)) {
-            failed = true;
-            break;
-          }
+        named_bar_sync(kPfBarV, kPfBarKVThreads);
+        for (int t = 0; t < 2; ++t) {
+          named_bar_sync(kPfBarP + t, kPfBarPThreads);
           tc_fence_after();
           // O_t += P_t V_j; P_t: TMEM columns [128 t, 128 t + 64), 16 keys per 8 columns
 #pragma unroll
-          for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-            const uint32_t a_tmem = tmem + t * kPfKeys + kk * 8;
-            const uint64_t bdesc =
-                umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes, 1024);
-            asm volatile(
-                "{\n"
-                "  .reg .pred p;\n"
-                "  setp.ne.b32 p, %4, 0;\n"
-                "  tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
-                "}\n" ::"r"(tmem + 256 + t * D),
-                "r"(a_tmem), "l"(bdesc), "r"(idesc_o), "r"((j > 0 || kk > 0) ? 1u : 0u)
-                : "memory");
-          }
-          umma_commit(&o_done[t]);
-          if (t == 1) umma_commit(&v_empty[st]);
+          for (int kk = 0; kk < kPfKeys / 16; ++kk)
+            umma_f16_ts_if(
+                issue, tmem + 256 + t * D, tmem + t * kPfKeys + kk * 8,
+                umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes, 1024),
+                idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_if(issue, &o_done[t]);
+          if (t == 1) umma_commit_if(issue, &v_empty[st]);
           // the next S_t overwrites P_t only after this PV (same issuing thread, in order)
           if (j + 1 < ntiles) issue_s(t, j + 1);
         }
       }
-      if (failed) set_status(PA_ERR_TIMEOUT);
+      // every MMA done before the TMEM is released
+      umma_commit_if(issue, mma_done);
+      if (!mbar_wait_warp(mma_done, 0)) failed = true;
+      if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
     }
-  } else if (warp >= 10) {
+  } else if (warp == kPfRelayWarp) {
+    regs_dec<kPfRegsOther>();
+    // ------------------------------------------------------------ relay
+    // Waits for each K / V tile's TMA completion and meets the issuer on a
+    // named barrier, in the order the issuer needs them (K_0, V_0, K_1, ...).
+    // After a timeout it keeps meeting the issuer so no barrier is left
+    // short of arrivals.
+    bool rfail = false;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % S;
+      if (!rfail && !mbar_wait_warp(&k_full[st], (j / S) & 1)) rfail = true;
+      named_bar_sync(kPfBarK, kPfBarKVThreads);
+      if (!rfail && !mbar_wait_warp(&v_full[st], (j / S) & 1)) rfail = true;
+      named_bar_sync(kPfBarV, kPfBarKVThreads);
+    }
+    if (rfail && lane == 0) set_status(PA_ERR_TIMEOUT);
+  } else if (warp > kPfRelayWarp) {
     regs_dec<kPfRegsOther>();
   } else {
     regs_inc<kPfRegsSoftmax>();
@@ -455,7 +473,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t tO = tmem + lane_addr + 256 + t * D;
     float m_used = -INFINITY, l = 0.f;
     float s[kPfKeys];
+    // Every step ends with this warpgroup meeting the issuer on the P_t
+    // barrier, also after a timeout (the work is skipped then), so every
+    // named barrier of the item completes.
     for (int j = 0; j < ntiles; ++j) {
+      if (!failed) do {
       if (!mbar_wait_warp(&s_full[t], j & 1)) {
         failed = true;
         break;
@@ -537,9 +559,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         fence_proxy_async();
       }
+      } while (false);
       tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      // bar.sync, not arrive: the warpgroup meets the issuer once per step
+      // and can never run a step ahead of it (it would have nothing to do:
+      // the next scores come after this PV).
+      named_bar_sync(kPfBarP + t, kPfBarPThreads);
     }
     // ---- epilogue: O_t / l -> out, LSE
     if (!failed && ntiles > 0) {
