@@ -384,60 +384,71 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == kPfMmaWarp) {
     regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ tcgen05 issuer
-    // The whole warp runs this loop (it takes part in the named barriers);
-    // lane 0 issues, as predicated instructions. The issuing thread touches
-    // no shared memory between MMAs: with only a couple of MMAs queued, a
-    // shared-memory wait on this thread would idle the tensor pipe. Its
-    // hand-offs are named barriers: P_t from softmax warpgroup t, K / V
-    // tiles from the relay warp.
-    const uint32_t issue = lane == 0 ? 1u : 0u;
+    // The whole warp runs this loop and takes part in the named barriers
+    // (hand-offs: P_t from softmax warpgroup t, K / V tiles from the relay
+    // warp); lane 0 issues the MMAs. The issuing thread touches no shared
+    // memory between MMAs: with only a couple of MMAs queued, a
+    // shared-memory wait on this thread would idle the tensor pipe.
     if (ntiles > 0) {
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_s = umma_idesc_f16(ab, kPfRows, kPfKeys, 0);
       const uint32_t idesc_o = umma_idesc_f16(ab, kPfRows, D, 1);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
       if (!mbar_wait_warp(q_full, 0)) failed = true;
-      // S_t = Q_t K_j^T into TMEM columns [128 t, 128 t + 128)
+      // S_t = Q_t K_j^T into TMEM columns [128 t, 128 t + 128); lane 0 only
       auto issue_s = [&](int t, int j) {
         const int st = j % S;
-        if (t == 0) {
-          named_bar_sync(kPfBarK, kPfBarKVThreads);
-          tc_fence_after();
-        }
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
-          umma_f16_if(issue, tmem + t * kPfKeys,
-                      umma_desc_sw128(q_base + t * C::kQBytes + off, 16, 1024),
-                      umma_desc_sw128(k_base + st * C::kTileBytes + off, 16, 1024), idesc_s,
-                      kk > 0 ? 1u : 0u);
+          umma_f16(tmem + t * kPfKeys, umma_desc_sw128(q_base + t * C::kQBytes + off, 16, 1024),
+                   umma_desc_sw128(k_base + st * C::kTileBytes + off, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
         }
-        umma_commit_if(issue, &s_full[t]);
-        if (t == 1) umma_commit_if(issue, &k_empty[st]);
+        umma_commit(&s_full[t]);
+        if (t == 1) umma_commit(&k_empty[st]);
       };
-      issue_s(0, 0);
-      issue_s(1, 0);
+      named_bar_sync(kPfBarK, kPfBarKVThreads);
+      if (lane == 0) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      __syncwarp();
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % S;
         named_bar_sync(kPfBarV, kPfBarKVThreads);
         for (int t = 0; t < 2; ++t) {
           named_bar_sync(kPfBarP + t, kPfBarPThreads);
-          tc_fence_after();
-          // O_t += P_t V_j; P_t: TMEM columns [128 t, 128 t + 64), 16 keys per 8 columns
+          if (t == 0 && j + 1 < ntiles) named_bar_sync(kPfBarK, kPfBarKVThreads);
+          if (lane == 0) {
+            tc_fence_after();
+            // O_t += P_t V_j; P_t: TMEM columns [128 t, 128 t + 64), 16 keys per 8 columns
 #pragma unroll
-          for (int kk = 0; kk < kPfKeys / 16; ++kk)
-            umma_f16_ts_if(
-                issue, tmem + 256 + t * D, tmem + t * kPfKeys + kk * 8,
-                umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes, 1024),
-                idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit_if(issue, &o_done[t]);
-          if (t == 1) umma_commit_if(issue, &v_empty[st]);
-          // the next S_t overwrites P_t only after this PV (same issuing thread, in order)
-          if (j + 1 < ntiles) issue_s(t, j + 1);
+            for (int kk = 0; kk < kPfKeys / 16; ++kk) {
+              asm volatile(
+                  "{\n"
+                  "  .reg .pred p;\n"
+                  "  setp.ne.b32 p, %4, 0;\n"
+                  "  tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+                  "}\n" ::"r"(tmem + 256 + t * D),
+                  "r"(tmem + t * kPfKeys + kk * 8),
+                  "l"(umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes,
+                                      1024)),
+                  "r"(idesc_o), "r"((j > 0 || kk > 0) ? 1u : 0u)
+                  : "memory");
+            }
+            umma_commit(&o_done[t]);
+            if (t == 1) umma_commit(&v_empty[st]);
+            // the next S_t overwrites P_t only after this PV (same thread, in order)
+            if (j + 1 < ntiles) issue_s(t, j + 1);
+          }
+          __syncwarp();
         }
       }
       // every MMA done before the TMEM is released
-      umma_commit_if(issue, mma_done);
+      if (lane == 0) umma_commit(mma_done);
+      __syncwarp();
       if (!mbar_wait_warp(mma_done, 0)) failed = true;
       if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
     }
