@@ -326,48 +326,4 @@ __device__ __forceinline__ void regs_inc() {
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
-
-// tcgen05.mma / commit issued only where `issue` is non-zero, as a predicated
-// instruction: a whole warp can run the issuing loop (and take part in named
-// barriers) without diverging, with one lane actually issuing.
-__device__ __forceinline__ void umma_f16_if(uint32_t issue, uint32_t d_tmem, uint64_t a_desc,
-                                            uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n"
-      "  .reg .pred p, q;\n"
-      "  setp.ne.b32 p, %4, 0;\n"
-      "  setp.ne.b32 q, %5, 0;\n"
-      "  @q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
-      "}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
-      : "memory");
-}
-// As umma_f16_if with the A operand in TMEM.
-__device__ __forceinline__ void umma_f16_ts_if(uint32_t issue, uint32_t d_tmem, uint32_t a_tmem,
-                                               uint64_t b_desc, uint32_t idesc,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n"
-      "  .reg .pred p, q;\n"
-      "  setp.ne.b32 p, %4, 0;\n"
-      "  setp.ne.b32 q, %5, 0;\n"
-      "  @q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
-      "}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
-      : "memory");
-}
-__device__ __forceinline__ void umma_commit_if(uint32_t issue, uint64_t* bar) {
-  asm volatile(
-      "{\n"
-      "  .reg .pred q;\n"
-      "  setp.ne.b32 q, %1, 0;\n"
-      "  @q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n"
-      "}\n" ::"r"(smem_u32(bar)),
-      "r"(issue)
-      : "memory");
-}
-
 }  // namespace pa

@@ -14,14 +14,20 @@
 //   * warp 8  — TMA producer: both Q tiles once (3-D map over [tokens, heads,
 //     dim], 128-byte swizzle), then K and V tiles of 8 pages (128 keys) into
 //     separate rings, each page one box per 64-column panel.
-//   * warp 9  — tcgen05 issuer (one thread), per K/V tile j and Q tile t:
-//     S_t = Q_t K_j^T (fp32, TMEM), then O_t += P_t V_j with P_t read from
-//     TMEM (bf16 / fp16 written over S_t's columns) and V_j from shared
-//     memory; completion reported through tcgen05.commit on mbarriers.
+//   * warp 9  — tcgen05 issuer (lane 0), per K/V tile j and Q tile t:
+//     in order O_t += P_t V_j then S_t(j+1) = Q_t K_{j+1}^T, with
+//     P_t read from TMEM (bf16 / fp16 written over S_t's columns) and V from
+//     shared memory; completion reported through tcgen05.commit on mbarriers.
+//     It never waits on shared memory between MMAs (the tensor pipe queues
+//     only a couple of MMAs, so any such wait would idle it): its hand-offs
+//     are named barriers.
+//   * warp 10 — relay: waits for each K / V tile's TMA completion and meets
+//     the issuer on a named barrier.
 //   * warps 0-3 / 4-7 — softmax + epilogue of Q tile 0 / 1, one thread per
 //     row (= TMEM lane): causal / length mask, online softmax in base 2 with
 //     lazy O rescaling (only when a row's max grows by more than 2^8), P back
-//     into TMEM; finally O is normalised and stored.
+//     into TMEM, then a named barrier with the issuer; finally O is
+//     normalised and stored.
 #pragma once
 
 #include "pa_common.cuh"
