@@ -111,6 +111,24 @@ int pa_apply_rope_pos_ids_inplace(void* q, int64_t q_stride_n, int64_t q_stride_
                                   int32_t head_dim, int32_t rotary_dim, int32_t interleave,
                                   float rope_scale, float rope_theta, int32_t dtype, void* stream);
 
+/* Replaces the reference's per-layer pair (src/models/llama.py:175-210)
+ *   flashinfer.apply_rope_pos_ids_inplace(q, k, positions, ...)
+ *   flashinfer.append_paged_kv_cache(k, v, batch_indices, positions, cache, ...)
+ * with one launch: q and k are rotated in place exactly as
+ * pa_apply_rope_pos_ids_inplace does (bit-identical rows), and the rotated k
+ * and v rows are written into their page slots exactly as
+ * pa_append_paged_kv_cache does (same slot rule, same device checks, padding
+ * rows with batch index -1 rotated but not appended). The cache dtype is the
+ * q / k / v dtype. Rows that are not 16-byte aligned or rotary_dim not a
+ * multiple of 16 take the two separate kernels, with the same results. */
+int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* k,
+                         int64_t k_stride_n, int64_t k_stride_h, const void* v,
+                         int64_t v_stride_n, int64_t v_stride_h, const int32_t* batch_indices,
+                         const int32_t* positions, int32_t nnz, int32_t num_qo_heads,
+                         int32_t rotary_dim, int32_t interleave, float rope_scale,
+                         float rope_theta, const pa_kv_cache* cache, const int32_t* kv_indices,
+                         const int32_t* kv_indptr, int32_t batch_size, void* stream);
+
 /* Workspace bytes pa_decode_plan needs for this batch geometry. */
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim);

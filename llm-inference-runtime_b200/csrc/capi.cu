@@ -319,6 +319,85 @@ int pa_apply_rope_pos_ids_inplace(void* q, int64_t q_stride_n, int64_t q_stride_
   return launch_status();
 }
 
+int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* k,
+                         int64_t k_stride_n, int64_t k_stride_h, const void* v,
+                         int64_t v_stride_n, int64_t v_stride_h, const int32_t* batch_indices,
+                         const int32_t* positions, int32_t nnz, int32_t num_qo_heads,
+                         int32_t rotary_dim, int32_t interleave, float rope_scale,
+                         float rope_theta, const pa_kv_cache* cache, const int32_t* kv_indices,
+                         const int32_t* kv_indptr, int32_t batch_size, void* stream) {
+  if (nnz < 0 || batch_size < 0 || num_qo_heads < 0) return PA_ERR_INVALID_ARGUMENT;
+  if (nnz == 0) return PA_OK;
+  if (cache == nullptr || q == nullptr || k == nullptr || v == nullptr ||
+      batch_indices == nullptr || positions == nullptr || kv_indices == nullptr ||
+      kv_indptr == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(cache->dtype)) return PA_ERR_UNSUPPORTED;
+  const int D = cache->head_dim, hkv = cache->num_kv_heads;
+  if (cache->k_base == nullptr || cache->v_base == nullptr || cache->page_size <= 0 || hkv <= 0 ||
+      D <= 0 || D % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (rotary_dim <= 0 || rotary_dim % 2 || rotary_dim > D) return PA_ERR_INVALID_ARGUMENT;
+  if (!(rope_scale > 0.f) || !(rope_theta > 0.f)) return PA_ERR_INVALID_ARGUMENT;
+  const bool fused = rotary_dim % 16 == 0 && aligned16(q) && aligned16(k) && aligned16(v) &&
+                     aligned16(cache->k_base) && aligned16(cache->v_base) && q_stride_n % 8 == 0 &&
+                     q_stride_h % 8 == 0 && k_stride_n % 8 == 0 && k_stride_h % 8 == 0 &&
+                     v_stride_n % 8 == 0 && v_stride_h % 8 == 0 && cache->page_stride % 8 == 0 &&
+                     cache->head_stride % 8 == 0 && cache->token_stride % 8 == 0;
+  if (!fused) {
+    const int rc = pa_apply_rope_pos_ids_inplace(q, q_stride_n, q_stride_h, k, k_stride_n,
+                                                 k_stride_h, positions, nnz, num_qo_heads, hkv, D,
+                                                 rotary_dim, interleave, rope_scale, rope_theta,
+                                                 cache->dtype, stream);
+    if (rc != PA_OK) return rc;
+    return pa_append_paged_kv_cache(k, k_stride_n, k_stride_h, v, v_stride_n, v_stride_h,
+                                    batch_indices, positions, nnz, cache, kv_indices, kv_indptr,
+                                    batch_size, stream);
+  }
+  RopeAppendParams p;
+  p.q = static_cast<uint8_t*>(q);
+  p.k = static_cast<uint8_t*>(k);
+  p.v = static_cast<const uint8_t*>(v);
+  p.q_sn = q_stride_n * 2;
+  p.q_sh = q_stride_h * 2;
+  p.k_sn = k_stride_n * 2;
+  p.k_sh = k_stride_h * 2;
+  p.v_sn = v_stride_n * 2;
+  p.v_sh = v_stride_h * 2;
+  p.batch_indices = batch_indices;
+  p.positions = positions;
+  p.nnz = nnz;
+  p.hq = num_qo_heads;
+  p.hkv = hkv;
+  p.head_dim = D;
+  p.rotary_dim = rotary_dim;
+  p.interleave = interleave ? 1 : 0;
+  p.inv_scale = 1.0f / rope_scale;
+  p.log2_theta = std::log2(rope_theta);
+  p.k_base = static_cast<uint8_t*>(const_cast<void*>(cache->k_base));
+  p.v_base = static_cast<uint8_t*>(const_cast<void*>(cache->v_base));
+  p.page_stride = cache->page_stride * 2;
+  p.head_stride = cache->head_stride * 2;
+  p.token_stride = cache->token_stride * 2;
+  p.num_pages = cache->num_pages;
+  p.kv_indices = kv_indices;
+  p.kv_indptr = kv_indptr;
+  p.batch = batch_size;
+  p.page_size = cache->page_size;
+  const int64_t per_token = static_cast<int64_t>(num_qo_heads + hkv) * (rotary_dim / 16) +
+                            static_cast<int64_t>(hkv) * ((D - rotary_dim) / 8 + D / 8);
+  const int64_t work = per_token * nnz;
+  const int dev = current_device();
+  const int64_t max_blocks = static_cast<int64_t>(sm_count(dev) > 0 ? sm_count(dev) : 148) * 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cache->dtype == PA_DTYPE_BF16)
+    rope_append_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
+  else
+    rope_append_kernel<__half><<<blocks, 256, 0, st>>>(p);
+  return launch_status();
+}
+
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim) {
   (void)num_qo_heads;

@@ -95,7 +95,21 @@ __global__ void append_kernel(const AppendParams p) {
 // flashinfer.apply_rope_pos_ids_inplace (src/models/llama.py:175-182):
 // for i < rotary_dim / 2, angle = pos / rope_scale * rope_theta^(-2i/rotary_dim).
 // Non-interleaved pairs (i, i + rotary_dim/2); interleaved pairs (2i, 2i+1).
-// One thread rotates one pair of one row; fp32 math, result rounded to T.
+// fp32 math, result rounded to T. The standalone kernel and the fused
+// RoPE + append kernel share these two functions (no FMA contraction), so
+// both paths give bit-identical rows.
+__device__ __forceinline__ void rope_cos_sin(int pos, int i, int rotary_dim, float inv_scale,
+                                             float log2_theta, float* cs, float* sn) {
+  const float freq = exp2f(-(2.0f * i / rotary_dim) * log2_theta) * inv_scale;
+  sincosf(static_cast<float>(pos) * freq, sn, cs);
+}
+__device__ __forceinline__ void rope_rotate(float x0, float x1, float cs, float sn, float* y0,
+                                            float* y1) {
+  *y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+  *y1 = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x0, sn));
+}
+
+// One thread rotates one pair of one row.
 template <typename T>
 __global__ void rope_kernel(T* q, int64_t q_sn, int64_t q_sh, T* k, int64_t k_sn, int64_t k_sh,
                             const int32_t* __restrict__ pos_ids, int nnz, int hq, int hkv,
@@ -110,16 +124,143 @@ __global__ void rope_kernel(T* q, int64_t q_sn, int64_t q_sh, T* k, int64_t k_sn
     const int head = rem / half;
     const int i = rem - head * half;
     T* row = head < hq ? q + t * q_sn + head * q_sh : k + t * k_sn + (head - hq) * k_sh;
-    const float freq = exp2f(-(2.0f * i / rotary_dim) * log2_theta) * inv_scale;
-    const float ang = static_cast<float>(__ldg(pos_ids + t)) * freq;
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
+    float cs, sn;
+    rope_cos_sin(__ldg(pos_ids + t), i, rotary_dim, inv_scale, log2_theta, &cs, &sn);
     const int a = interleave ? 2 * i : i;
     const int bidx = interleave ? 2 * i + 1 : i + half;
-    const float x0 = static_cast<float>(row[a]);
-    const float x1 = static_cast<float>(row[bidx]);
-    row[a] = static_cast<T>(x0 * cs - x1 * sn);
-    row[bidx] = static_cast<T>(x1 * cs + x0 * sn);
+    float y0, y1;
+    rope_rotate(static_cast<float>(row[a]), static_cast<float>(row[bidx]), cs, sn, &y0, &y1);
+    row[a] = static_cast<T>(y0);
+    row[bidx] = static_cast<T>(y1);
+  }
+}
+
+// ------------------------------------------------------- RoPE + append
+// The reference's per-layer pair apply_rope_pos_ids_inplace(q, k, positions)
+// then append_paged_kv_cache(k, v, batch_indices, positions, ...)
+// (src/models/llama.py:175-210) in one pass: q and k are rotated in place
+// and the rotated k and v rows are written into their page slots, so k is
+// read once instead of three times. Work units per token: 8 rotary pairs of
+// a q head or a k head (two 16-byte chunks), a 16-byte chunk of k past
+// rotary_dim, a 16-byte chunk of v. Needs rotary_dim % 16 == 0 and 16-byte
+// aligned rows (the host entry point checks).
+struct RopeAppendParams {
+  uint8_t* q;
+  uint8_t* k;
+  const uint8_t* v;
+  int64_t q_sn, q_sh, k_sn, k_sh, v_sn, v_sh;  // bytes
+  const int32_t* batch_indices;
+  const int32_t* positions;
+  int nnz, hq, hkv, head_dim, rotary_dim, interleave;
+  float inv_scale, log2_theta;
+  uint8_t* k_base;
+  uint8_t* v_base;
+  int64_t page_stride, head_stride, token_stride;  // bytes
+  int64_t num_pages;
+  const int32_t* kv_indices;
+  const int32_t* kv_indptr;
+  int batch, page_size;
+};
+
+// Page slot of token t's row of kv head h (nullptr: padding row or an error,
+// recorded in the status word).
+__device__ __forceinline__ int64_t rope_append_slot(const RopeAppendParams& p, int t, int h) {
+  const int b = __ldg(p.batch_indices + t);
+  if (b < 0) return -1;  // padding row (batch index -1): rotated, not appended
+  const int pos = __ldg(p.positions + t);
+  if (b >= p.batch || pos < 0) {
+    set_status(PA_ERR_DEVICE_CHECK);
+    return -1;
+  }
+  const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
+  const int pi = start + pos / p.page_size;
+  if (pi >= end) {
+    set_status(PA_ERR_DEVICE_CHECK);
+    return -1;
+  }
+  const int page = __ldg(p.kv_indices + pi);
+  if (page < 0 || page >= p.num_pages) {
+    set_status(PA_ERR_DEVICE_CHECK);
+    return -1;
+  }
+  return page * p.page_stride + h * p.head_stride + (pos % p.page_size) * p.token_stride;
+}
+
+template <typename T>
+__device__ __forceinline__ void rope_chunk8(uint4* lo, uint4* hi, int pos, int i0, int interleave,
+                                            const RopeAppendParams& p) {
+  // lo / hi: two 16-byte chunks holding 8 pairs: non-interleaved lo[e] pairs
+  // with hi[e]; interleaved the 16 elements lo|hi are 8 adjacent pairs.
+  T* a = reinterpret_cast<T*>(lo);
+  T* b = reinterpret_cast<T*>(hi);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float cs, sn, y0, y1;
+    rope_cos_sin(pos, i0 + e, p.rotary_dim, p.inv_scale, p.log2_theta, &cs, &sn);
+    T* x0 = interleave ? (e < 4 ? a + 2 * e : b + 2 * (e - 4)) : a + e;
+    T* x1 = interleave ? x0 + 1 : b + e;
+    rope_rotate(static_cast<float>(*x0), static_cast<float>(*x1), cs, sn, &y0, &y1);
+    *x0 = static_cast<T>(y0);
+    *x1 = static_cast<T>(y1);
+  }
+}
+
+template <typename T>
+__global__ void rope_append_kernel(const RopeAppendParams p) {
+  const int nrot = p.rotary_dim / 16;              // 8-pair units per head
+  const int npass = (p.head_dim - p.rotary_dim) / 8;  // k chunks past rotary_dim
+  const int nv = p.head_dim / 8;                   // v chunks
+  const int64_t per_token =
+      static_cast<int64_t>(p.hq + p.hkv) * nrot + static_cast<int64_t>(p.hkv) * (npass + nv);
+  const int64_t total = per_token * p.nnz;
+  const int half = p.rotary_dim / 2;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(idx / per_token);
+    int u = static_cast<int>(idx - t * per_token);
+    if (u < (p.hq + p.hkv) * nrot) {
+      // rotary unit: 8 pairs of a q or k head
+      const int head = u / nrot, c = u - head * nrot;
+      const bool is_k = head >= p.hq;
+      const int h = is_k ? head - p.hq : head;
+      uint8_t* row = is_k ? p.k + t * p.k_sn + h * p.k_sh : p.q + t * p.q_sn + h * p.q_sh;
+      // element offsets of the two chunks
+      const int e_lo = p.interleave ? 16 * c : 8 * c;
+      const int e_hi = p.interleave ? 16 * c + 8 : half + 8 * c;
+      uint4* lo_ptr = reinterpret_cast<uint4*>(row + e_lo * 2);
+      uint4* hi_ptr = reinterpret_cast<uint4*>(row + e_hi * 2);
+      uint4 lo = *lo_ptr, hi = *hi_ptr;
+      rope_chunk8<T>(&lo, &hi, __ldg(p.positions + t), 8 * c, p.interleave, p);
+      *lo_ptr = lo;
+      *hi_ptr = hi;
+      if (is_k) {
+        const int64_t off = rope_append_slot(p, t, h);
+        if (off >= 0) {
+          *reinterpret_cast<uint4*>(p.k_base + off + e_lo * 2) = lo;
+          *reinterpret_cast<uint4*>(p.k_base + off + e_hi * 2) = hi;
+        }
+      }
+      continue;
+    }
+    u -= (p.hq + p.hkv) * nrot;
+    if (u < p.hkv * npass) {
+      // k chunk past rotary_dim: copied as is
+      const int h = u / npass, c = u - h * npass;
+      const int e = p.rotary_dim + 8 * c;
+      const int64_t off = rope_append_slot(p, t, h);
+      if (off >= 0)
+        *reinterpret_cast<uint4*>(p.k_base + off + e * 2) =
+            *reinterpret_cast<const uint4*>(p.k + t * p.k_sn + h * p.k_sh + e * 2);
+      continue;
+    }
+    u -= p.hkv * npass;
+    {
+      const int h = u / nv, c = u - h * nv;
+      const int64_t off = rope_append_slot(p, t, h);
+      if (off >= 0)
+        *reinterpret_cast<uint4*>(p.v_base + off + c * 16) =
+            __ldg(reinterpret_cast<const uint4*>(p.v + t * p.v_sn + h * p.v_sh) + c);
+    }
   }
 }
 

@@ -196,6 +196,43 @@ def apply_rope_pos_ids_inplace(q: torch.Tensor, k: torch.Tensor, pos_ids: torch.
     _after("apply_rope_pos_ids_inplace")
 
 
+def apply_rope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      batch_indices: torch.Tensor, positions: torch.Tensor, paged_kv_cache,
+                      kv_indices: torch.Tensor, kv_indptr: torch.Tensor,
+                      kv_last_page_len: torch.Tensor, kv_layout: str = "NHD",
+                      rotary_dim: Optional[int] = None, interleave: bool = False,
+                      rope_scale: float = 1, rope_theta: float = 1e4) -> None:
+    """apply_rope_pos_ids_inplace(q, k, positions, ...) followed by
+    append_paged_kv_cache(k, v, batch_indices, positions, ...), in one launch
+    (the pair the reference runs per layer at src/models/llama.py:175-210).
+    Same results as the two calls: q and k rotated in place, the rotated k and
+    v written into their page slots."""
+    desc = kv_cache_desc(paged_kv_cache, kv_layout)
+    if not (q.dtype == k.dtype == v.dtype) or _dtype_code(q.dtype) != desc.dtype:
+        raise ValueError("q / k / v must have the KV cache's dtype")
+    qsn, qsh = _row_strides(q, "q")
+    ksn, ksh = _row_strides(k, "k")
+    vsn, vsh = _row_strides(v, "v")
+    if k.shape != v.shape or k.size(1) != desc.num_kv_heads or k.size(2) != desc.head_dim:
+        raise ValueError("k / v shape does not match the KV cache")
+    if q.size(0) != k.size(0) or q.size(2) != k.size(2):
+        raise ValueError("q and k must have the same rows and head_dim")
+    d = q.size(-1)
+    if rotary_dim is None:
+        rotary_dim = d
+    device = q.device
+    batch_indices = _i32_on(batch_indices, device, "batch_indices")
+    positions = _i32_on(positions, device, "positions")
+    kv_indices = _i32_on(kv_indices, device, "kv_indices")
+    kv_indptr = _i32_on(kv_indptr, device, "kv_indptr")
+    _lib.check(_lib.load().pa_apply_rope_append(
+        _p(q), qsn, qsh, _p(k), ksn, ksh, _p(v), vsn, vsh, _p(batch_indices), _p(positions),
+        q.size(0), q.size(1), rotary_dim, int(bool(interleave)), float(rope_scale),
+        float(rope_theta), ctypes.byref(desc), _p(kv_indices), _p(kv_indptr),
+        kv_indptr.numel() - 1, _stream()), "apply_rope_append")
+    _after("apply_rope_append")
+
+
 # -------------------------------------------------------------------- merge
 def merge_states(v: torch.Tensor, s: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """v [n, S, H, D], s [n, S, H] (float32, base-2 LSE) -> merged (v, s)."""

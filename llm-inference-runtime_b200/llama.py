@@ -119,19 +119,19 @@ def paged_attention(attn, q_flat: torch.Tensor, k_flat: torch.Tensor,
     projections (llama.py:173-245). Returns [rows, H_q, D].
     """
     positions = cast(torch.Tensor, PagedAttnState.positions)
-    flashinfer.apply_rope_pos_ids_inplace(q_flat, k_flat, positions,
-                                          rope_theta=attn.rope_theta,
-                                          rope_scale=attn.rope_scale, interleave=False)
     kv_pool = cast(torch.Tensor, PagedAttnState.kv_pool)
     layer_kv_cache = kv_pool[attn.layer_idx]
-    flashinfer.append_paged_kv_cache(
-        append_key=k_flat, append_value=v_flat,
+    # RoPE on q / k and the KV append in one launch; same results as the
+    # reference's apply_rope_pos_ids_inplace + append_paged_kv_cache pair.
+    flashinfer.apply_rope_append(
+        q_flat, k_flat, v_flat,
         batch_indices=cast(torch.Tensor, PagedAttnState.batch_indices),
         positions=positions, paged_kv_cache=layer_kv_cache,
         kv_indices=cast(torch.Tensor, PagedAttnState.kv_indices),
         kv_indptr=cast(torch.Tensor, PagedAttnState.kv_indptr),
         kv_last_page_len=cast(torch.Tensor, PagedAttnState.kv_last_page_len),
-        kv_layout="HND")
+        kv_layout="HND", rope_theta=attn.rope_theta, rope_scale=attn.rope_scale,
+        interleave=False)
     if PagedAttnState.mode == "prefill":
         pw = cast(flashinfer.BatchPrefillWithPagedKVCacheWrapper, PagedAttnState.prefill_wrapper)
         return pw.forward(q=q_flat, paged_kv_cache=layer_kv_cache, causal=True)

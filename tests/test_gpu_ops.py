@@ -127,3 +127,104 @@ def test_merge_states_matches_float64(fi):
                             lse[:, 1].to(DEV))
     wv2, ws2 = paged_kv.merge_states(v[:, :2].float().numpy(), lse[:, :2].numpy())
     assert np.abs(va.cpu().float().numpy() - wv2).max() < 2e-2
+
+
+def _rope_append_case(rng, layout, hkv, d, hq=32, dtype=torch.bfloat16):
+    P, N = 16, 300
+    chunk = np.array([37, 1, 200, 16, 5])
+    prefix = np.array([0, 15, 100, 32, 4000])
+    seq = prefix + chunk
+    npages = (seq + P - 1) // P
+    indptr = np.concatenate([[0], np.cumsum(npages)]).astype(np.int32)
+    indices = rng.permutation(N)[: indptr[-1]].astype(np.int32)
+    last = (seq - (npages - 1) * P).astype(np.int32)
+    shape = (N, 2, hkv, P, d) if layout == "HND" else (N, 2, P, hkv, d)
+    pool = torch.from_numpy(rng.standard_normal(shape, dtype=np.float32)).to(dtype)
+    nnz = int(chunk.sum()) + 3  # three padding rows (batch index -1)
+    qkv = torch.from_numpy(rng.standard_normal((nnz, (hq + 2 * hkv) * d),
+                                               dtype=np.float32)).to(dtype)
+    append_indptr = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    bi, pos = paged_kv.batch_indices_positions(append_indptr, seq, nnz)
+    return dict(pool=pool, qkv=qkv, bi=bi, pos=pos, indices=indices, indptr=indptr, last=last,
+                hq=hq, nnz=nnz)
+
+
+@pytest.mark.parametrize("layout", ["HND", "NHD"])
+@pytest.mark.parametrize("hkv,d,rotary", [(4, 64, None), (8, 128, None), (8, 128, 64)])
+@pytest.mark.parametrize("interleave", [False, True])
+def test_rope_append_fused_equals_separate_calls(fi, layout, hkv, d, rotary, interleave):
+    """The fused RoPE + append is bit-identical to RoPE followed by append,
+    for q / k rotated in place (strided views of one fused QKV buffer) and
+    for every pool byte; padding rows are rotated but not appended."""
+    c = _rope_append_case(np.random.default_rng(hkv * d + (rotary or 0)), layout, hkv, d)
+    hq, nnz = c["hq"], c["nnz"]
+    runs = []
+    for fused in (False, True):
+        qkv = c["qkv"].to(DEV)
+        pool = c["pool"].to(DEV)
+        q, k, v = qkv.split([hq * d, hkv * d, hkv * d], dim=-1)
+        q, k, v = q.view(nnz, hq, d), k.view(nnz, hkv, d), v.view(nnz, hkv, d)
+        args = dict(batch_indices=_t(c["bi"]), positions=_t(c["pos"]), paged_kv_cache=pool,
+                    kv_indices=_t(c["indices"]), kv_indptr=_t(c["indptr"]),
+                    kv_last_page_len=_t(c["last"]), kv_layout=layout)
+        if fused:
+            fi.apply_rope_append(q, k, v, rotary_dim=rotary, interleave=interleave,
+                                 rope_theta=5e5, **args)
+        else:
+            fi.apply_rope_pos_ids_inplace(q, k, _t(c["pos"]), rotary_dim=rotary,
+                                          interleave=interleave, rope_theta=5e5)
+            fi.append_paged_kv_cache(k, v, **args)
+        runs.append((qkv.cpu(), pool.cpu()))
+    assert torch.equal(runs[0][0], runs[1][0])
+    assert torch.equal(runs[0][1], runs[1][1])
+    # and the pool equals the oracle's append of the rotated rows
+    qkv_rot = runs[1][0]
+    _, k_rot, v_rot = qkv_rot.split([hq * d, hkv * d, hkv * d], dim=-1)
+    want = c["pool"].clone()
+    paged_kv.append_paged_kv_cache(k_rot.reshape(nnz, hkv, d), v_rot.reshape(nnz, hkv, d),
+                                   c["bi"], c["pos"], want, c["indices"], c["indptr"],
+                                   layout=layout)
+    assert torch.equal(runs[1][1], want)
+
+
+def test_rope_append_fused_fp16_and_unaligned_fallback(fi):
+    """fp16, and a rotary_dim that is not a multiple of 16 (two-kernel path)."""
+    rng = np.random.default_rng(11)
+    for rotary in (None, 40):
+        c = _rope_append_case(rng, "HND", 4, 64, dtype=torch.float16)
+        hq, nnz, d, hkv = c["hq"], c["nnz"], 64, 4
+        outs = []
+        for fused in (False, True):
+            qkv = c["qkv"].to(DEV)
+            pool = c["pool"].to(DEV)
+            q, k, v = qkv.split([hq * d, hkv * d, hkv * d], dim=-1)
+            q, k, v = q.view(nnz, hq, d), k.view(nnz, hkv, d), v.view(nnz, hkv, d)
+            args = dict(batch_indices=_t(c["bi"]), positions=_t(c["pos"]), paged_kv_cache=pool,
+                        kv_indices=_t(c["indices"]), kv_indptr=_t(c["indptr"]),
+                        kv_last_page_len=_t(c["last"]), kv_layout="HND")
+            if fused:
+                fi.apply_rope_append(q, k, v, rotary_dim=rotary, **args)
+            else:
+                fi.apply_rope_pos_ids_inplace(q, k, _t(c["pos"]), rotary_dim=rotary)
+                fi.append_paged_kv_cache(k, v, **args)
+            outs.append((qkv.cpu(), pool.cpu()))
+        assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_rope_append_flags_out_of_range_position(fi, lir):
+    import importlib
+    fa = importlib.import_module("llm-inference-runtime_b200.flashinfer_api")
+    pool = torch.zeros(4, 2, 4, 16, 64, dtype=torch.bfloat16, device=DEV)
+    q = torch.ones(1, 32, 64, dtype=torch.bfloat16, device=DEV)
+    k = torch.ones(1, 4, 64, dtype=torch.bfloat16, device=DEV)
+    torch.cuda.synchronize()
+    lir._lib.device_status()
+    saved = fa._CHECK
+    fa._CHECK = False
+    try:
+        fi.apply_rope_append(q, k, k.clone(), _t([0]), _t([20]), pool, _t([2]), _t([0, 1]),
+                             _t([5]), kv_layout="HND")
+        assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
+    finally:
+        fa._CHECK = saved
+    assert torch.count_nonzero(pool) == 0
