@@ -129,6 +129,46 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
                          float rope_theta, const pa_kv_cache* cache, const int32_t* kv_indices,
                          const int32_t* kv_indptr, int32_t batch_size, void* stream);
 
+/* Replaces the Python table build of StepExecutor._run_decode
+ * (src/engine/runtime/step_executor.py:204-225) with a device build:
+ *   kv_indices = concatenation of each sequence's whole block table (the
+ *   first num_blocks[b] entries of row b of block_tables, rows
+ *   block_table_stride elements apart), kv_indptr its offsets,
+ *   kv_last_page_len[b] = seq_lens[b] % page_size or page_size,
+ *   batch_indices[b] = b, positions[b] = seq_lens[b] - 1.
+ * seq_lens is the sequence's get_len. counts (device int32[3]) receives
+ * {batch_size, batch_size, 0}. A table that cannot cover its length, or more
+ * pages than kv_indices_capacity, writes counts = {0, 0, 1} and records
+ * PA_ERR_DEVICE_CHECK. All inputs and outputs are device memory; two
+ * launches, no synchronisation (capturable in a CUDA graph). */
+int pa_build_decode_tables(const int32_t* block_tables, int64_t block_table_stride,
+                           const int32_t* num_blocks, const int32_t* seq_lens, int32_t batch_size,
+                           int32_t page_size, int32_t* kv_indptr, int32_t* kv_indices,
+                           int64_t kv_indices_capacity, int32_t* kv_last_page_len,
+                           int32_t* batch_indices, int32_t* positions, int32_t* counts,
+                           void* stream);
+
+/* Replaces the Python table build of StepExecutor._run_prefill
+ * (src/engine/runtime/step_executor.py:98-155) and the batch indices /
+ * positions it then requests (step_executor.py:155) with a device build.
+ * Per input sequence b: chunk = min(chunk_lens[b], prompt_lens[b] -
+ * computed_lens[b]); sequences with chunk <= 0 are dropped, the others fill
+ * output slots in input order (active[slot] = b) with
+ *   qo_indptr = offsets of the chunks, seq_lens[slot] = computed + chunk,
+ *   kv_indices = the first ceil(seq_lens / page_size) blocks of the table,
+ *   kv_last_page_len = seq_lens % page_size or page_size,
+ *   rows t of the chunk: batch_indices[t] = slot,
+ *   positions[t] = computed + (t - qo_indptr[slot]).
+ * counts (device int32[3]) receives {active sequences, rows, error flag}. */
+int pa_build_prefill_tables(const int32_t* block_tables, int64_t block_table_stride,
+                            const int32_t* num_blocks, const int32_t* prompt_lens,
+                            const int32_t* computed_lens, const int32_t* chunk_lens,
+                            int32_t batch_size, int32_t page_size, int32_t* qo_indptr,
+                            int32_t* kv_indptr, int32_t* kv_indices, int64_t kv_indices_capacity,
+                            int32_t* kv_last_page_len, int32_t* seq_lens, int32_t* active,
+                            int32_t* batch_indices, int32_t* positions, int64_t rows_capacity,
+                            int32_t* counts, void* stream);
+
 /* Workspace bytes pa_decode_plan needs for this batch geometry. */
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim);

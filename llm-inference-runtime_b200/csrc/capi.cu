@@ -12,6 +12,7 @@
 #include "decode.cuh"
 #include "ops.cuh"
 #include "prefill.cuh"
+#include "tables.cuh"
 
 namespace {
 
@@ -395,6 +396,88 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
     rope_append_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
   else
     rope_append_kernel<__half><<<blocks, 256, 0, st>>>(p);
+  return launch_status();
+}
+
+int pa_build_decode_tables(const int32_t* block_tables, int64_t block_table_stride,
+                           const int32_t* num_blocks, const int32_t* seq_lens, int32_t batch_size,
+                           int32_t page_size, int32_t* kv_indptr, int32_t* kv_indices,
+                           int64_t kv_indices_capacity, int32_t* kv_last_page_len,
+                           int32_t* batch_indices, int32_t* positions, int32_t* counts,
+                           void* stream) {
+  if (batch_size < 0 || page_size <= 0 || block_table_stride < 0 || kv_indices_capacity < 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (kv_indptr == nullptr || counts == nullptr) return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size > 0 && (block_tables == nullptr || num_blocks == nullptr || seq_lens == nullptr ||
+                         kv_last_page_len == nullptr || batch_indices == nullptr ||
+                         positions == nullptr || (kv_indices_capacity > 0 && kv_indices == nullptr)))
+    return PA_ERR_INVALID_ARGUMENT;
+  TablesParams p{};
+  p.block_tables = block_tables;
+  p.stride = block_table_stride;
+  p.num_blocks = num_blocks;
+  p.lens = seq_lens;
+  p.batch = batch_size;
+  p.page_size = page_size;
+  p.prefill = 0;
+  p.kv_indptr = kv_indptr;
+  p.kv_indices = kv_indices;
+  p.kv_capacity = kv_indices_capacity;
+  p.last_page_len = kv_last_page_len;
+  p.batch_indices = batch_indices;
+  p.positions = positions;
+  p.rows_capacity = batch_size;
+  p.counts = counts;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  tables_scan_kernel<<<1, kTablesScanThreads, 0, st>>>(p);
+  if (batch_size > 0) tables_gather_kernel<<<batch_size, 128, 0, st>>>(p);
+  return launch_status();
+}
+
+int pa_build_prefill_tables(const int32_t* block_tables, int64_t block_table_stride,
+                            const int32_t* num_blocks, const int32_t* prompt_lens,
+                            const int32_t* computed_lens, const int32_t* chunk_lens,
+                            int32_t batch_size, int32_t page_size, int32_t* qo_indptr,
+                            int32_t* kv_indptr, int32_t* kv_indices, int64_t kv_indices_capacity,
+                            int32_t* kv_last_page_len, int32_t* seq_lens, int32_t* active,
+                            int32_t* batch_indices, int32_t* positions, int64_t rows_capacity,
+                            int32_t* counts, void* stream) {
+  if (batch_size < 0 || page_size <= 0 || block_table_stride < 0 || kv_indices_capacity < 0 ||
+      rows_capacity < 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (qo_indptr == nullptr || kv_indptr == nullptr || counts == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size > 0 &&
+      (block_tables == nullptr || num_blocks == nullptr || prompt_lens == nullptr ||
+       computed_lens == nullptr || chunk_lens == nullptr || kv_last_page_len == nullptr ||
+       seq_lens == nullptr || active == nullptr ||
+       (kv_indices_capacity > 0 && kv_indices == nullptr) ||
+       (rows_capacity > 0 && (batch_indices == nullptr || positions == nullptr))))
+    return PA_ERR_INVALID_ARGUMENT;
+  TablesParams p{};
+  p.block_tables = block_tables;
+  p.stride = block_table_stride;
+  p.num_blocks = num_blocks;
+  p.lens = computed_lens;
+  p.prompt_lens = prompt_lens;
+  p.chunk_lens = chunk_lens;
+  p.batch = batch_size;
+  p.page_size = page_size;
+  p.prefill = 1;
+  p.qo_indptr = qo_indptr;
+  p.kv_indptr = kv_indptr;
+  p.kv_indices = kv_indices;
+  p.kv_capacity = kv_indices_capacity;
+  p.last_page_len = kv_last_page_len;
+  p.seq_lens_out = seq_lens;
+  p.active = active;
+  p.batch_indices = batch_indices;
+  p.positions = positions;
+  p.rows_capacity = rows_capacity;
+  p.counts = counts;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  tables_scan_kernel<<<1, kTablesScanThreads, 0, st>>>(p);
+  if (batch_size > 0) tables_gather_kernel<<<batch_size, 128, 0, st>>>(p);
   return launch_status();
 }
 
