@@ -169,6 +169,21 @@ int pa_build_prefill_tables(const int32_t* block_tables, int64_t block_table_str
                             int32_t* batch_indices, int32_t* positions, int64_t rows_capacity,
                             int32_t* counts, void* stream);
 
+/* Copy-on-write fork of pages (the reference plans it for shared partial
+ * pages, todo.md "Incremental Radix Cache Insertion & Copy-on-Write"; its
+ * allocator, src/engine/memory/allocator.py, has no fork yet): for every
+ * pair i and layer l, the page_bytes bytes at
+ *   pool + l * layer_stride_bytes + src_pages[i] * page_stride_bytes
+ * are copied to the same place of page dst_pages[i]. For the engine's pool
+ * [L, N, 2, H_kv, P, D] a page of a layer (K and V of every head) is one
+ * contiguous block: page_bytes = page_stride_bytes = 2 * H_kv * P * D * elem.
+ * dst pages must be distinct and not among the sources. Page ids outside
+ * [0, num_pages) are skipped and recorded as PA_ERR_DEVICE_CHECK. */
+int pa_fork_pages(void* pool, int64_t layer_stride_bytes, int32_t num_layers,
+                  int64_t page_stride_bytes, int64_t page_bytes, int64_t num_pages,
+                  const int32_t* src_pages, const int32_t* dst_pages, int32_t num_pairs,
+                  void* stream);
+
 /* Workspace bytes pa_decode_plan needs for this batch geometry. */
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim);

@@ -481,6 +481,34 @@ int pa_build_prefill_tables(const int32_t* block_tables, int64_t block_table_str
   return launch_status();
 }
 
+int pa_fork_pages(void* pool, int64_t layer_stride_bytes, int32_t num_layers,
+                  int64_t page_stride_bytes, int64_t page_bytes, int64_t num_pages,
+                  const int32_t* src_pages, const int32_t* dst_pages, int32_t num_pairs,
+                  void* stream) {
+  if (num_pairs < 0 || num_layers < 0 || num_pages < 0) return PA_ERR_INVALID_ARGUMENT;
+  if (num_pairs == 0 || num_layers == 0 || page_bytes == 0) return PA_OK;
+  if (pool == nullptr || src_pages == nullptr || dst_pages == nullptr) return PA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(pool) || page_bytes % 16 || page_stride_bytes % 16 || layer_stride_bytes % 16 ||
+      page_bytes < 0 || page_bytes > page_stride_bytes)
+    return PA_ERR_INVALID_ARGUMENT;
+  ForkParams p;
+  p.pool = static_cast<uint8_t*>(pool);
+  p.layer_stride = layer_stride_bytes;
+  p.page_stride = page_stride_bytes;
+  p.page_bytes = page_bytes;
+  p.num_layers = num_layers;
+  p.num_pages = num_pages;
+  p.src = src_pages;
+  p.dst = dst_pages;
+  p.n = num_pairs;
+  const int64_t work = (page_bytes / 16) * num_layers * static_cast<int64_t>(num_pairs);
+  const int dev = current_device();
+  const int64_t max_blocks = static_cast<int64_t>(sm_count(dev) > 0 ? sm_count(dev) : 148) * 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
+  fork_pages_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim) {
   (void)num_qo_heads;

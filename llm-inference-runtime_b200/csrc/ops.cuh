@@ -264,6 +264,43 @@ __global__ void rope_append_kernel(const RopeAppendParams p) {
   }
 }
 
+// ------------------------------------------------------------ page fork
+// Copy-on-write of shared partial pages (the reference's planned incremental
+// radix insertion, todo.md "Copy-on-Write"): before a sequence appends into
+// a page another sequence still references, the page is forked — its bytes
+// in every layer copied to a fresh page id — and the sequence's block table
+// then points at the copy. One thread per 16-byte chunk of (pair, layer).
+struct ForkParams {
+  uint8_t* pool;
+  int64_t layer_stride, page_stride, page_bytes;  // bytes
+  int num_layers;
+  int64_t num_pages;
+  const int32_t* src;
+  const int32_t* dst;
+  int n;
+};
+
+__global__ void fork_pages_kernel(const ForkParams p) {
+  const int64_t chunks = p.page_bytes / 16;
+  const int64_t per_pair = chunks * p.num_layers;
+  const int64_t total = per_pair * p.n;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx / per_pair);
+    const int64_t rem = idx - i * per_pair;
+    const int layer = static_cast<int>(rem / chunks);
+    const int64_t c = rem - layer * chunks;
+    const int s = __ldg(p.src + i), d = __ldg(p.dst + i);
+    if (s < 0 || s >= p.num_pages || d < 0 || d >= p.num_pages) {
+      set_status(PA_ERR_DEVICE_CHECK);
+      continue;
+    }
+    const uint8_t* from = p.pool + layer * p.layer_stride + s * p.page_stride;
+    uint8_t* to = p.pool + layer * p.layer_stride + d * p.page_stride;
+    reinterpret_cast<uint4*>(to)[c] = reinterpret_cast<const uint4*>(from)[c];
+  }
+}
+
 // -------------------------------------------------------------- merge
 // flashinfer.merge_states: v [n, S, H, D], s [n, S, H] (base-2 LSE) ->
 // v_merged [n, H, D], s_merged [n, H]. One warp per (row, head).

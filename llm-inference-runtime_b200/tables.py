@@ -105,3 +105,22 @@ def build_prefill_tables(block_tables: torch.Tensor, num_blocks: torch.Tensor,
         _p(out["batch_indices"]), _p(out["positions"]), rows, _p(out["counts"]), _stream()),
         "build_prefill_tables")
     return out
+
+
+def fork_pages(kv_pool: torch.Tensor, src_pages: torch.Tensor, dst_pages: torch.Tensor) -> None:
+    """Copy-on-write fork: page src_pages[i] -> dst_pages[i] in every layer of
+    the engine's pool [L, N, 2, H_kv, P, D] (or one layer [N, 2, H_kv, P, D]),
+    K and V of every head. dst pages must be distinct and not sources."""
+    pool = kv_pool if kv_pool.dim() == 6 else kv_pool.unsqueeze(0)
+    if pool.dim() != 6 or not pool.is_cuda:
+        raise ValueError("kv_pool must be [L, N, 2, H_kv, P, D] (or one layer) on the GPU")
+    if pool[0, 0].is_contiguous() is False or pool.stride(1) != pool[0, 0].numel():
+        raise ValueError("each page of a layer must be one contiguous block")
+    src = _i32(src_pages, "src_pages")
+    dst = _i32(dst_pages, "dst_pages")
+    if src.numel() != dst.numel():
+        raise ValueError("src_pages and dst_pages must have the same length")
+    es = pool.element_size()
+    _lib.check(_lib.load().pa_fork_pages(
+        _p(pool), pool.stride(0) * es, pool.size(0), pool.stride(1) * es, pool[0, 0].numel() * es,
+        pool.size(1), _p(src), _p(dst), src.numel(), _stream()), "fork_pages")

@@ -190,3 +190,25 @@ def test_decode_step_from_device_tables_captured_in_cuda_graph(tb, fi, workloads
     torch.cuda.synchronize()
     assert torch.equal(short, out)
     assert not torch.equal(short, eager)
+
+
+@pytest.mark.parametrize("layers", [1, 22])
+def test_fork_pages_copies_every_layer_bit_exact(tb, layers):
+    g = torch.Generator().manual_seed(layers)
+    pool = torch.randn(layers, 64, 2, 4, 16, 64, generator=g).to(torch.bfloat16)
+    src = torch.tensor([3, 9, 9, 40], dtype=torch.int32)  # a page may be forked twice
+    dst = torch.tensor([10, 11, 50, 63], dtype=torch.int32)
+    want = pool.clone()
+    want[:, dst.long()] = pool[:, src.long()]
+    gpu = pool.to(DEV)
+    tb.fork_pages(gpu if layers > 1 else gpu[0], src.to(DEV), dst.to(DEV))
+    assert torch.equal(gpu.cpu(), want)
+
+
+def test_fork_pages_flags_out_of_range(tb, lir):
+    torch.cuda.synchronize()
+    lir._lib.device_status()
+    pool = torch.zeros(2, 8, 2, 4, 16, 64, dtype=torch.bfloat16, device=DEV)
+    tb.fork_pages(pool, _i([1]), _i([8]))
+    assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
+    assert torch.count_nonzero(pool) == 0
