@@ -6,7 +6,9 @@
 #include <type_traits>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <utility>
 #include <mutex>
 
 #include "decode.cuh"
@@ -124,6 +126,39 @@ int launch_status() {
   return e == cudaSuccess ? PA_OK : PA_ERR_CUDA;
 }
 
+// Kernels of the per-step chain (positions, plan, append, decode) launch with
+// programmatic stream serialization: each may start while its predecessor in
+// the stream drains and waits (griddepcontrol.wait) before reading its
+// inputs, which hides the launch gap between dependent kernels. PA_PDL=0 in
+// the environment turns it off (plain stream order).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("PA_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_chain(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                 cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return PA_ERR_CUDA;
+  }
+  return launch_status();
+}
+
 // Decode partition for a cache shape on device `dev`: one CTA per SM, each
 // holding DecodeGeom::groups_per_cta groups.
 struct DecodePlanShape {
@@ -155,8 +190,8 @@ int launch_decode(const CUtensorMap& km, const CUtensorMap& vm, const DecodePara
       return PA_ERR_CUDA;
     allowed[dev].store(sh.g.smem_bytes, std::memory_order_relaxed);
   }
-  decode_kernel<T, D><<<sh.ctas, sh.g.threads, sh.g.smem_bytes, stream>>>(km, vm, prm);
-  return launch_status();
+  return launch_chain(decode_kernel<T, D>, dim3(sh.ctas), dim3(sh.g.threads), sh.g.smem_bytes,
+                      stream, km, vm, prm);
 }
 
 // 3-D map over q [tokens, heads, dim] (strides in elements), box (64 dims,
@@ -228,9 +263,9 @@ int pa_batch_indices_positions(const int32_t* append_indptr, const int32_t* seq_
   if (append_indptr == nullptr || (batch_size > 0 && seq_lens == nullptr)) return PA_ERR_INVALID_ARGUMENT;
   if (nnz > 0 && (batch_indices == nullptr || positions == nullptr)) return PA_ERR_INVALID_ARGUMENT;
   if (nnz == 0) return PA_OK;
-  batch_indices_positions_kernel<<<batch_size + 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      append_indptr, seq_lens, batch_size, nnz, batch_indices, positions);
-  return launch_status();
+  return launch_chain(batch_indices_positions_kernel, dim3(batch_size + 1), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), append_indptr, seq_lens, batch_size, nnz,
+                      batch_indices, positions);
 }
 
 int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
@@ -282,8 +317,8 @@ int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64
   const int dev = current_device();
   const int64_t max_blocks = static_cast<int64_t>(sm_count(dev) > 0 ? sm_count(dev) : 148) * 8;
   const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
-  append_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status();
+  return launch_chain(append_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                      p);
 }
 
 int pa_apply_rope_pos_ids_inplace(void* q, int64_t q_stride_n, int64_t q_stride_h, void* k,
@@ -393,10 +428,8 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
   const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cache->dtype == PA_DTYPE_BF16)
-    rope_append_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(p);
-  else
-    rope_append_kernel<__half><<<blocks, 256, 0, st>>>(p);
-  return launch_status();
+    return launch_chain(rope_append_kernel<__nv_bfloat16>, dim3(blocks), dim3(256), 0, st, p);
+  return launch_chain(rope_append_kernel<__half>, dim3(blocks), dim3(256), 0, st, p);
 }
 
 int pa_build_decode_tables(const int32_t* block_tables, int64_t block_table_stride,
@@ -538,10 +571,10 @@ int pa_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, in
     return dev < 0 ? PA_ERR_CUDA : PA_ERR_UNSUPPORTED;
   if (decode_ws_bytes(sh, batch_size, num_kv_heads, head_dim) > workspace_bytes)
     return PA_ERR_WORKSPACE_TOO_SMALL;
-  decode_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-      kv_indptr, kv_last_page_len, batch_size, num_kv_heads, num_qo_heads, head_dim, page_size,
-      num_kv_indices, sh.units, sh.g.hb, /*min_per_group=*/4, static_cast<uint8_t*>(workspace));
-  return launch_status();
+  return launch_chain(decode_plan_kernel, dim3(1), dim3(1024), 0,
+                      static_cast<cudaStream_t>(stream), kv_indptr, kv_last_page_len, batch_size,
+                      num_kv_heads, num_qo_heads, head_dim, page_size, num_kv_indices, sh.units,
+                      sh.g.hb, /*min_per_group=*/4, static_cast<uint8_t*>(workspace));
 }
 
 int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,

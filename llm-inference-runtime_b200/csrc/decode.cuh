@@ -94,6 +94,8 @@ __global__ void decode_plan_kernel(const int32_t* __restrict__ kv_indptr,
                                    int hq, int head_dim, int page_size, int64_t num_indices,
                                    int num_groups, int hb, int min_per_group,
                                    uint8_t* __restrict__ ws) {
+  griddep_wait();
+  griddep_launch_dependents();
   const DecodeWsLayout L = decode_ws_layout(num_groups, batch, hkv, head_dim, hb);
   DecodePlanHeader* hdr = reinterpret_cast<DecodePlanHeader*>(ws + L.hdr);
   int4* unit_start = reinterpret_cast<int4*>(ws + L.unit_start);
@@ -266,6 +268,9 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  // everything above is private to this CTA; from here on the plan and the
+  // pool (which the previous kernel may have written) are read
+  griddep_wait();
 
   if (hdr->magic != kDecodeMagic || hdr->num_units != num_groups ||
       hdr->batch_size != p.batch_size || hdr->num_kv_heads != p.num_kv_heads ||
@@ -568,6 +573,10 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
       phase ^= 1;
     }
   }
+
+  // the next kernel in the stream may start its prologue (it waits for this
+  // grid's completion before reading anything)
+  griddep_launch_dependents();
 
   if (n_pend > 0) {
     // Publish this warp's partials, then count its pieces; the warp that

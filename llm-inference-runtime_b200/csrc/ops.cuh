@@ -16,6 +16,8 @@ __global__ void batch_indices_positions_kernel(const int32_t* __restrict__ appen
                                                const int32_t* __restrict__ seq_lens, int batch,
                                                int nnz, int32_t* __restrict__ batch_indices,
                                                int32_t* __restrict__ positions) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.x;
   if (b < batch) {
     const int start = append_indptr[b], end = min(append_indptr[b + 1], nnz);
@@ -54,6 +56,8 @@ struct AppendParams {
 // V: page = kv_indices[kv_indptr[b] + pos / P], slot = pos % P. The
 // reference's call site is src/models/llama.py:188-210 (kv_layout "HND").
 __global__ void append_kernel(const AppendParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t per_token = static_cast<int64_t>(p.num_kv_heads) * p.row_chunks * 2;
   const int64_t total = per_token * p.nnz;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -207,6 +211,8 @@ __device__ __forceinline__ void rope_chunk8(uint4* lo, uint4* hi, int pos, int i
 
 template <typename T>
 __global__ void rope_append_kernel(const RopeAppendParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int nrot = p.rotary_dim / 16;              // 8-pair units per head
   const int npass = (p.head_dim - p.rotary_dim) / 8;  // k chunks past rotary_dim
   const int nv = p.head_dim / 8;                   // v chunks

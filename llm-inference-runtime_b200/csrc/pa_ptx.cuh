@@ -323,6 +323,19 @@ __device__ __forceinline__ void regs_inc() {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running; griddep_wait() blocks until that kernel has completed and its
+// memory is visible, so it must precede every read of data the previous
+// kernel may have produced. griddep_launch_dependents() lets the next such
+// kernel start its own prologue early.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
