@@ -184,6 +184,27 @@ int pa_fork_pages(void* pool, int64_t layer_stride_bytes, int32_t num_layers,
                   const int32_t* src_pages, const int32_t* dst_pages, int32_t num_pairs,
                   void* stream);
 
+/* Replaces the per-layer prologue of the reference's patched attention
+ * (src/models/llama.py:163-210): qkv = x W^T with W the fused [q; k; v]
+ * projection weight of _fuse_qkv_proj_plain (llama.py:256-280, no bias),
+ * RoPE on the q and k heads (apply_rope_pos_ids_inplace), and the append of
+ * k and v into the paged cache (append_paged_kv_cache) — one tcgen05 GEMM
+ * whose epilogue rotates in fp32 straight from the accumulator.
+ *   x       [num_tokens, hidden], row stride x_stride elements
+ *   weight  [(H_q + 2 H_kv) * D, hidden], row stride w_stride elements
+ *   q_out   [num_tokens, H_q, D] rotated q, token stride q_stride_n elements
+ * k / v rows of token t go to the slot of (batch_indices[t], positions[t])
+ * exactly as pa_append_paged_kv_cache places them (batch index -1: not
+ * appended). RoPE uses positions[t]. Values match the unfused sequence up to
+ * the one rounding of qkv to 16 bits that the fusion removes. Needs D = 64
+ * or 128, hidden % 64 == 0 and H_q * D, H_kv * D multiples of 128. */
+int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int64_t w_stride,
+                       int32_t num_tokens, int32_t hidden, int32_t num_qo_heads, void* q_out,
+                       int64_t q_stride_n, const int32_t* batch_indices, const int32_t* positions,
+                       int32_t rotary_dim, int32_t interleave, float rope_scale, float rope_theta,
+                       const pa_kv_cache* cache, const int32_t* kv_indices,
+                       const int32_t* kv_indptr, int32_t batch_size, void* stream);
+
 /* Workspace bytes pa_decode_plan needs for this batch geometry. */
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim);

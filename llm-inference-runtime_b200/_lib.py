@@ -90,6 +90,12 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int32, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int32,
          c_void_p],
     ),
+    "pa_qkv_rope_append": (
+        c_int32,
+        [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64,
+         c_void_p, c_void_p, c_int32, c_int32, c_float, c_float, POINTER(PagedKVCache), c_void_p,
+         c_void_p, c_int32, c_void_p],
+    ),
     "pa_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "pa_decode_plan": (
         c_int32,

@@ -15,6 +15,7 @@
 #include "ops.cuh"
 #include "prefill.cuh"
 #include "tables.cuh"
+#include "qkv.cuh"
 
 namespace {
 
@@ -105,6 +106,25 @@ int encode_kv_map(CUtensorMap* map, const void* base, const pa_kv_cache& c, int 
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// 2-D map over a row-major matrix [rows, cols] (row stride in elements), box
+// (64 columns, box_rows rows), 128-byte swizzle: the K-major operand tile of
+// a tcgen05 GEMM. Rows past the end read as zeros.
+int encode_2d_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                  int64_t row_stride, int box_rows, int dtype) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return PA_ERR_CUDA;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? PA_OK : PA_ERR_INVALID_ARGUMENT;
+}
 
 bool valid_dtype(int dt) { return dt == PA_DTYPE_F16 || dt == PA_DTYPE_BF16; }
 
@@ -540,6 +560,94 @@ int pa_fork_pages(void* pool, int64_t layer_stride_bytes, int32_t num_layers,
   const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, max_blocks));
   fork_pages_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return launch_status();
+}
+
+int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int64_t w_stride,
+                       int32_t num_tokens, int32_t hidden, int32_t num_qo_heads, void* q_out,
+                       int64_t q_stride_n, const int32_t* batch_indices, const int32_t* positions,
+                       int32_t rotary_dim, int32_t interleave, float rope_scale, float rope_theta,
+                       const pa_kv_cache* cache, const int32_t* kv_indices,
+                       const int32_t* kv_indptr, int32_t batch_size, void* stream) {
+  if (num_tokens < 0 || hidden <= 0 || num_qo_heads <= 0 || batch_size < 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return PA_OK;
+  if (x == nullptr || weight == nullptr || q_out == nullptr || cache == nullptr ||
+      batch_indices == nullptr || positions == nullptr || kv_indices == nullptr ||
+      kv_indptr == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(cache->dtype)) return PA_ERR_UNSUPPORTED;
+  const int D = cache->head_dim, hkv = cache->num_kv_heads;
+  if (D != 64 && D != 128) return PA_ERR_UNSUPPORTED;
+  if (cache->k_base == nullptr || cache->v_base == nullptr || cache->page_size <= 0 || hkv <= 0)
+    return PA_ERR_INVALID_ARGUMENT;
+  // tiles of 128 columns never straddle the q / k / v column ranges
+  if ((num_qo_heads * D) % 128 || (hkv * D) % 128 || hidden % kQkvBK)
+    return PA_ERR_UNSUPPORTED;
+  if (rotary_dim <= 0 || rotary_dim % 2 || rotary_dim > D) return PA_ERR_INVALID_ARGUMENT;
+  if (!(rope_scale > 0.f) || !(rope_theta > 0.f)) return PA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(q_out) || !aligned16(cache->k_base) ||
+      !aligned16(cache->v_base) || x_stride % 8 || w_stride % 8 || q_stride_n % 8 ||
+      x_stride < hidden || w_stride < hidden || q_stride_n < static_cast<int64_t>(num_qo_heads) * D ||
+      cache->page_stride % 8 || cache->head_stride % 8 || cache->token_stride % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  const int64_t N = static_cast<int64_t>(num_qo_heads + 2 * hkv) * D;
+  CUtensorMap xm, wm;
+  int rc = encode_2d_map(&xm, x, num_tokens, hidden, x_stride, kQkvBM, cache->dtype);
+  if (rc != PA_OK) return rc;
+  QkvParams p;
+  p.M = num_tokens;
+  p.K = hidden;
+  p.hq = num_qo_heads;
+  p.hkv = hkv;
+  p.head_dim = D;
+  p.q_out = static_cast<uint8_t*>(q_out);
+  p.q_sn = q_stride_n * 2;
+  p.batch_indices = batch_indices;
+  p.positions = positions;
+  p.rotary_dim = rotary_dim;
+  p.interleave = interleave ? 1 : 0;
+  p.inv_scale = 1.0f / rope_scale;
+  p.log2_theta = std::log2(rope_theta);
+  p.k_base = static_cast<uint8_t*>(const_cast<void*>(cache->k_base));
+  p.v_base = static_cast<uint8_t*>(const_cast<void*>(cache->v_base));
+  p.page_stride = cache->page_stride * 2;
+  p.head_stride = cache->head_stride * 2;
+  p.token_stride = cache->token_stride * 2;
+  p.num_pages = cache->num_pages;
+  p.kv_indices = kv_indices;
+  p.kv_indptr = kv_indptr;
+  p.batch = batch_size;
+  p.page_size = cache->page_size;
+  const int dev = current_device();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // few tokens: weight-streaming tiles (N=128, 6 stages); many: N=256
+  const bool wide = num_tokens > 512 && N % 256 == 0 && (num_qo_heads * D) % 256 == 0 &&
+                    (hkv * D) % 256 == 0;
+  const int bn = wide ? 256 : 128;
+  rc = encode_2d_map(&wm, weight, N, hidden, w_stride, bn, cache->dtype);
+  if (rc != PA_OK) return rc;
+  const dim3 grid(static_cast<unsigned>((num_tokens + kQkvBM - 1) / kQkvBM),
+                  static_cast<unsigned>(N / bn));
+  const bool bf = cache->dtype == PA_DTYPE_BF16;
+  auto go = [&](auto kernel, int smem, std::atomic<uint64_t>* done) -> int {
+    if (allow_smem(kernel, smem, done, dev) != cudaSuccess) return PA_ERR_CUDA;
+    kernel<<<grid, kQkvThreads, smem, st>>>(xm, wm, p);
+    return launch_status();
+  };
+  static std::atomic<uint64_t> done[8];
+  using N6 = QkvCfg<128, 6>;
+  using W3 = QkvCfg<256, 3>;
+  if (bf && D == 64)
+    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 64, 256, 3>, W3::kSmemBytes, &done[0])
+                : go(qkv_rope_append_kernel<__nv_bfloat16, 64, 128, 6>, N6::kSmemBytes, &done[1]);
+  if (bf)
+    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 128, 256, 3>, W3::kSmemBytes, &done[2])
+                : go(qkv_rope_append_kernel<__nv_bfloat16, 128, 128, 6>, N6::kSmemBytes, &done[3]);
+  if (D == 64)
+    return wide ? go(qkv_rope_append_kernel<__half, 64, 256, 3>, W3::kSmemBytes, &done[4])
+                : go(qkv_rope_append_kernel<__half, 64, 128, 6>, N6::kSmemBytes, &done[5]);
+  return wide ? go(qkv_rope_append_kernel<__half, 128, 256, 3>, W3::kSmemBytes, &done[6])
+              : go(qkv_rope_append_kernel<__half, 128, 128, 6>, N6::kSmemBytes, &done[7]);
 }
 
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,

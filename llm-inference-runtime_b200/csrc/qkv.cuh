@@ -1,0 +1,264 @@
+// Fused QKV projection -> RoPE -> KV append, sm_100a tcgen05.
+//
+// The reference's per-layer prologue of the patched attention
+// (src/models/llama.py:163-210): qkv = x W^T with W the fused
+// [q_proj; k_proj; v_proj] weight (_fuse_qkv_proj_plain, llama.py:256-280,
+// no bias), split into q, k, v; RoPE on q and k
+// (apply_rope_pos_ids_inplace); k and v scattered into their page slots
+// (append_paged_kv_cache). Here one GEMM kernel does all of it: each CTA
+// computes a 128-token x BN-column tile of qkv in TMEM and its epilogue
+// rotates the q / k heads of the tile in fp32 straight from the fp32
+// accumulator and stores q rows to the q buffer and k / v rows to the pool,
+// so qkv never goes to memory.
+//
+// Per CTA (192 threads):
+//   * warp 4 — TMA producer: x tile [128 tokens x 64] and W tile
+//     [BN columns x 64] per 64-deep k block into a ring (both K-major,
+//     128-byte swizzle).
+//   * warp 5 — tcgen05 issuer: 4 MMAs (M=128, N=BN, K=16) per k block into
+//     BN TMEM columns; tcgen05.commit frees the stage.
+//   * warps 0-3 — epilogue, one thread per token row (= TMEM lane).
+#pragma once
+
+#include "pa_common.cuh"
+#include "ops.cuh"
+
+namespace pa {
+
+constexpr int kQkvBM = 128, kQkvBK = 64;
+constexpr int kQkvThreads = 192;
+// Tile shapes: N=128 columns with a deep 6-stage ring for few tokens (the
+// GEMM then streams the weight: more CTAs, more bytes in flight per CTA);
+// N=256 columns for many tokens (MMAs of 128 cycles keep the issuer's
+// per-stage barrier wait hidden behind the queued MMAs).
+template <int BN, int STAGES>
+struct QkvCfg {
+  static constexpr int kStageBytes = (kQkvBM + BN) * kQkvBK * 2;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 256 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct QkvParams {
+  int M, K, hq, hkv, head_dim;
+  uint8_t* q_out;
+  int64_t q_sn;  // bytes between token rows of q_out (heads contiguous, head_dim apart)
+  const int32_t* batch_indices;
+  const int32_t* positions;
+  int rotary_dim, interleave;
+  float inv_scale, log2_theta;
+  uint8_t* k_base;
+  uint8_t* v_base;
+  int64_t page_stride, head_stride, token_stride;  // bytes
+  int64_t num_pages;
+  const int32_t* kv_indices;
+  const int32_t* kv_indptr;
+  int batch, page_size;
+};
+
+// Page slot of token m's row of kv head h, or -1 (padding row / error).
+__device__ __forceinline__ int64_t qkv_slot(const QkvParams& p, int m, int h) {
+  const int b = __ldg(p.batch_indices + m);
+  if (b < 0) return -1;
+  const int pos = __ldg(p.positions + m);
+  if (b >= p.batch || pos < 0) {
+    set_status(PA_ERR_DEVICE_CHECK);
+    return -1;
+  }
+  const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
+  const int pi = start + pos / p.page_size;
+  if (pi >= end) {
+    set_status(PA_ERR_DEVICE_CHECK);
+    return -1;
+  }
+  const int page = __ldg(p.kv_indices + pi);
+  if (page < 0 || page >= p.num_pages) {
+    set_status(PA_ERR_DEVICE_CHECK);
+    return -1;
+  }
+  return page * p.page_stride + h * p.head_stride + (pos % p.page_size) * p.token_stride;
+}
+
+template <typename T, int D, int BN, int STAGES>
+__global__ void __launch_bounds__(kQkvThreads, 1)
+    qkv_rope_append_kernel(const __grid_constant__ CUtensorMap xmap,
+                           const __grid_constant__ CUtensorMap wmap, const QkvParams p) {
+  constexpr int S = STAGES;
+  constexpr int kStageBytes = QkvCfg<BN, STAGES>::kStageBytes;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kQkvBM, n0 = blockIdx.y * BN;
+  const int nk = p.K / kQkvBK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&xmap);
+    prefetch_tensormap(&wmap);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool failed = false;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int st = kb % S;
+        if (kb >= S && !mbar_wait(&empty[st], ((kb / S) - 1) & 1)) {
+          failed = true;
+          break;
+        }
+        uint8_t* sa = smem + st * kStageBytes;
+        mbar_arrive_expect_tx(&full[st], kStageBytes);
+        tma_load_2d(sa, &xmap, &full[st], kb * kQkvBK, m0);
+        tma_load_2d(sa + kQkvBM * kQkvBK * 2, &wmap, &full[st], kb * kQkvBK, n0);
+      }
+      if (failed) set_status(PA_ERR_TIMEOUT);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ tcgen05 issuer
+    if (lane == 0) {
+      const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      const uint32_t idesc = umma_idesc_f16(ab, kQkvBM, BN, 0);
+      const uint32_t base = smem_u32(smem);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int st = kb % S;
+        if (!mbar_wait(&full[st], (kb / S) & 1)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = base + st * kStageBytes, sb = sa + kQkvBM * kQkvBK * 2;
+#pragma unroll
+        for (int kk = 0; kk < kQkvBK / 16; ++kk)
+          umma_f16(tmem, umma_desc_sw128(sa + kk * 32, 16, 1024),
+                   umma_desc_sw128(sb + kk * 32, 16, 1024), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[st]);
+      }
+      // on a timeout the accumulator is garbage; the epilogue still runs
+      // (bounded) and the status word says so
+      umma_commit(acc_full);
+      if (failed) set_status(PA_ERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int r = warp * 32 + lane;  // tile row == TMEM lane
+    const int m = m0 + r;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const bool ok = mbar_wait_warp(acc_full, 0);
+    if (!ok) {
+      if (lane == 0) set_status(PA_ERR_TIMEOUT);
+    } else {
+      tc_fence_after();
+      constexpr int HPT = BN / D;  // heads per tile
+      const int qcols = p.hq * D, kcols = p.hkv * D;
+      const int region = n0 < qcols ? 0 : (n0 < qcols + kcols ? 1 : 2);  // q / k / v
+      const int head0 = region == 0 ? n0 / D : (region == 1 ? (n0 - qcols) / D
+                                                             : (n0 - qcols - kcols) / D);
+      const int pos = m < p.M ? __ldg(p.positions + m) : 0;
+      const bool active = m < p.M;
+      // RoPE angles depend on (position, pair) only: each thread tabulates
+      // cos / sin for its token once, in the stage memory the main loop no
+      // longer needs (column r of [2 * half][128] floats, read back only by
+      // this thread), and every q / k head of the tile reuses them. Code
+      // that runs once per CTA stays small: the epilogue is instruction-
+      // fetch bound when straight-line.
+      float* tab = reinterpret_cast<float*>(smem);
+      const int half = p.rotary_dim / 2;
+      if (region < 2) {
+#pragma unroll 1
+        for (int i = 0; i < half; ++i) {
+          float cs, sn;
+          rope_cos_sin(pos, i, p.rotary_dim, p.inv_scale, p.log2_theta, &cs, &sn);
+          tab[i * kQkvBM + r] = cs;
+          tab[(half + i) * kQkvBM + r] = sn;
+        }
+      }
+#pragma unroll 1
+      for (int hh = 0; hh < HPT; ++hh) {
+        float a[D];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) tmem_ld32(taddr + hh * D + c * 32, a + c * 32);
+        tmem_wait_ld();
+        if (region < 2 && active) {
+          // fp32 rotation of the accumulator (rope_rotate, as rope_kernel)
+          if (p.rotary_dim == D && !p.interleave) {
+#pragma unroll
+            for (int i = 0; i < D / 2; ++i) {
+              float y0, y1;
+              rope_rotate(a[i], a[i + D / 2], tab[i * kQkvBM + r], tab[(D / 2 + i) * kQkvBM + r],
+                          &y0, &y1);
+              a[i] = y0;
+              a[i + D / 2] = y1;
+            }
+          } else if (p.rotary_dim == D) {
+#pragma unroll
+            for (int i = 0; i < D / 2; ++i) {
+              float y0, y1;
+              rope_rotate(a[2 * i], a[2 * i + 1], tab[i * kQkvBM + r],
+                          tab[(D / 2 + i) * kQkvBM + r], &y0, &y1);
+              a[2 * i] = y0;
+              a[2 * i + 1] = y1;
+            }
+          } else {
+            float tmp[D];
+#pragma unroll
+            for (int e = 0; e < D; ++e) tmp[e] = a[e];
+#pragma unroll 1
+            for (int i = 0; i < half; ++i) {
+              float y0, y1;
+              const int ia = p.interleave ? 2 * i : i, ib = p.interleave ? 2 * i + 1 : i + half;
+              rope_rotate(tmp[ia], tmp[ib], tab[i * kQkvBM + r], tab[(half + i) * kQkvBM + r],
+                          &y0, &y1);
+              tmp[ia] = y0;
+              tmp[ib] = y1;
+            }
+#pragma unroll
+            for (int e = 0; e < D; ++e) a[e] = tmp[e];
+          }
+        }
+        // pack pairs in place over a[0 .. D/2)
+#pragma unroll
+        for (int e = 0; e < D / 2; ++e) a[e] = __uint_as_float(pack2<T>(a[2 * e], a[2 * e + 1]));
+        uint8_t* dst = nullptr;
+        if (active && region == 0) {
+          dst = p.q_out + m * p.q_sn + static_cast<int64_t>(head0 + hh) * D * 2;
+        } else if (active) {
+          const int64_t off = qkv_slot(p, m, head0 + hh);
+          if (off >= 0) dst = (region == 1 ? p.k_base : p.v_base) + off;
+        }
+        if (dst != nullptr) {
+#pragma unroll
+          for (int e = 0; e < D / 8; ++e)
+            reinterpret_cast<uint4*>(dst)[e] =
+                make_uint4(__float_as_uint(a[4 * e]), __float_as_uint(a[4 * e + 1]),
+                           __float_as_uint(a[4 * e + 2]), __float_as_uint(a[4 * e + 3]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+}  // namespace pa

@@ -19,12 +19,20 @@ attributes: one engine per process, one device per process.
 
 from __future__ import annotations
 
+import os
 from typing import Optional, cast
 
 import torch
 from torch import nn
 
 from . import flashinfer_api as flashinfer
+from . import fused
+
+# The fused QKV projection kernel (one launch: GEMM + RoPE + KV append) is
+# opt-in: on a B200 it loses to cuBLAS + the fused RoPE/append kernel in GPU
+# time (decode-sized batches: 20-34 vs 10-13 us; 8192 tokens: 433 vs 360 us)
+# while saving one launch. PA_FUSED_QKV=1 turns it on.
+_FUSED_QKV = os.environ.get("PA_FUSED_QKV", "0") == "1"
 
 
 class PagedAttnState:
@@ -139,18 +147,49 @@ def paged_attention(attn, q_flat: torch.Tensor, k_flat: torch.Tensor,
     return dw.forward(q=q_flat, paged_kv_cache=layer_kv_cache)
 
 
+def paged_attention_fused(attn, x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """As paged_attention, starting from the layer input: the fused QKV
+    projection kernel produces the rotated q and appends k / v, then the
+    prefill or decode attention runs. Returns [rows, H_q, D]."""
+    kv_pool = cast(torch.Tensor, PagedAttnState.kv_pool)
+    layer_kv_cache = kv_pool[attn.layer_idx]
+    q_flat = fused.qkv_rope_append(
+        x, weight, attn.num_heads,
+        batch_indices=cast(torch.Tensor, PagedAttnState.batch_indices),
+        positions=cast(torch.Tensor, PagedAttnState.positions),
+        paged_kv_cache=layer_kv_cache,
+        kv_indices=cast(torch.Tensor, PagedAttnState.kv_indices),
+        kv_indptr=cast(torch.Tensor, PagedAttnState.kv_indptr),
+        kv_layout="HND", rope_theta=attn.rope_theta, rope_scale=attn.rope_scale,
+        interleave=False)
+    if PagedAttnState.mode == "prefill":
+        pw = cast(flashinfer.BatchPrefillWithPagedKVCacheWrapper, PagedAttnState.prefill_wrapper)
+        return pw.forward(q=q_flat, paged_kv_cache=layer_kv_cache, causal=True)
+    dw = cast(flashinfer.BatchDecodeWithPagedKVCacheWrapper, PagedAttnState.decode_wrapper)
+    return dw.forward(q=q_flat, paged_kv_cache=layer_kv_cache)
+
+
 def patched_llama_attention_forward(self, hidden_states: torch.Tensor,
                                     position_embeddings=None, attention_mask=None,
                                     past_key_value=None, output_attentions=False,
                                     use_cache=False, cache_position=None, **kwargs):
     """Replacement LlamaAttention.forward (reference: llama.py:150-249)."""
     bsz, q_len, _ = hidden_states.shape
-    qkv = self.qkv_proj(hidden_states)
-    q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
-    q_flat = q.view(-1, self.num_heads, self.head_dim)
-    k_flat = k.view(-1, self.num_key_value_heads, self.head_dim)
-    v_flat = v.view(-1, self.num_key_value_heads, self.head_dim)
-    out = paged_attention(self, q_flat, k_flat, v_flat)
+    proj = self.qkv_proj
+    x = hidden_states.reshape(-1, hidden_states.size(-1))
+    if (_FUSED_QKV and isinstance(proj, torch.nn.Linear) and proj.bias is None
+            and x.stride(-1) == 1
+            and fused.supported(proj.weight, self.num_heads, self.num_key_value_heads,
+                                self.head_dim, x.dtype)):
+        # projection, RoPE and KV append in one kernel (qkv never stored)
+        out = paged_attention_fused(self, x, proj.weight)
+    else:
+        qkv = proj(hidden_states)
+        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+        q_flat = q.view(-1, self.num_heads, self.head_dim)
+        k_flat = k.view(-1, self.num_key_value_heads, self.head_dim)
+        v_flat = v.view(-1, self.num_key_value_heads, self.head_dim)
+        out = paged_attention(self, q_flat, k_flat, v_flat)
     if PagedAttnState.mode == "prefill":
         out = out.reshape(bsz, q_len, self.num_heads * self.head_dim)
     else:

@@ -47,8 +47,12 @@ def _close(got, want):
     return float(rel), float(cos)
 
 
-def test_patched_model_prefill_then_decode_matches_hf_eager(fi):
+@pytest.mark.parametrize("fused_qkv", [False, True])
+def test_patched_model_prefill_then_decode_matches_hf_eager(fi, monkeypatch, fused_qkv):
+    """fused_qkv: the projection + RoPE + append kernel instead of the
+    projection followed by the RoPE + append kernel."""
     llama = importlib.import_module("llm-inference-runtime_b200.llama")
+    monkeypatch.setattr(llama, "_FUSED_QKV", fused_qkv)
     ref = _model()
     ours = copy.deepcopy(ref)
     llama.patch_llama_model(ours)
