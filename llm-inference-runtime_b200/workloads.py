@@ -135,6 +135,46 @@ def make_decode_problem(geom: Geometry, batch: int, lo: int, hi: int, seed: int 
                          v_new=v_new.to(dtype).to(device), positions=lengths - 1)
 
 
+def make_shared_prefix_problem(geom: Geometry, batch: int = 64, prefix: int = 2048,
+                               lo: int = 32, hi: int = 256, seed: int = 0,
+                               device: str | torch.device = "cpu", dtype=torch.bfloat16,
+                               num_layers: int = 1) -> DecodeProblem:
+    """Configuration 4: `batch` requests whose tables start with the same
+    prefix / P page ids (the refcounted pages a radix-cache hit hands out),
+    followed by unique suffix pages for suffixes ~ U[lo, hi] (+1 appended
+    token). extra["unique_pages"] counts the distinct pages referenced."""
+    P = geom.page_size
+    assert prefix % P == 0
+    g = torch.Generator().manual_seed(seed)
+    suffix = torch.randint(lo, hi + 1, (batch,), generator=g).numpy().astype(np.int64) + 1
+    lengths = prefix + suffix
+    shared_pages = prefix // P
+    suffix_pages = (suffix + P - 1) // P
+    N = shared_pages + int(suffix_pages.sum())
+    perm = torch.randperm(N, generator=g).numpy().astype(np.int32)
+    shared = perm[:shared_pages]
+    rest = perm[shared_pages:]
+    tables, o = [], 0
+    for n in suffix_pages:
+        tables.append(np.concatenate([shared, rest[o:o + n]]))
+        o += n
+    indptr = np.zeros(batch + 1, dtype=np.int32)
+    np.cumsum([len(t) for t in tables], out=indptr[1:])
+    indices = np.concatenate(tables).astype(np.int32)
+    last = (suffix - (suffix_pages - 1) * P).astype(np.int32)
+    q = torch.randn((batch, geom.num_qo_heads, geom.head_dim), generator=g)
+    k_new = torch.randn((batch, geom.num_kv_heads, geom.head_dim), generator=g)
+    v_new = torch.randn((batch, geom.num_kv_heads, geom.head_dim), generator=g)
+    pool = torch.empty((num_layers, N, 2, geom.num_kv_heads, P, geom.head_dim), dtype=dtype,
+                       device=device)
+    _fill_normal(pool, seed + 1)
+    return DecodeProblem(geom=geom, lengths=lengths, kv_indptr=indptr, kv_indices=indices,
+                         kv_last_page_len=last, num_pages=N, pool=pool,
+                         q=q.to(dtype).to(device), k_new=k_new.to(dtype).to(device),
+                         v_new=v_new.to(dtype).to(device), positions=lengths - 1,
+                         extra={"unique_pages": N, "shared_pages": shared_pages})
+
+
 @dataclass
 class PrefillProblem:
     geom: Geometry
