@@ -373,4 +373,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # usage: python tests/golden/make_golden.py <checkout of the reference project>
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT")
+    main(sys.argv[1])
