@@ -488,6 +488,12 @@ def run_mixed(args):
         peak_tf = float(json.load(f)["bf16_tflops"])
     pre_tf = flops / (pre_ms * 1e-3) / 1e12
     dec_gbs = dbytes / (dec_ms * 1e-3) / 1e9
+    cpu, cpu_pre = None, None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import cpu_baseline as cb
+        cpu = cb.time_decode_sample(dec.lengths, geom, budget_s=8.0, sample=16)
+        cpu_pre = cb.time_prefill_sample(pre.qo_lens, pre.prefix_lens, geom, budget_s=8.0)
+    _barrier(world)
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -512,10 +518,11 @@ def run_mixed(args):
                                      "peak": peak_tf, "unit": "TFLOP/s",
                                      "frac": round(pre_tf / peak_tf, 4),
                                      "peak_kind": "measured (cuBLAS bf16 burst)",
-                                     "kernel": "prefill_kernel"}},
+                                     "kernel": "prefill_kernel"},
+                        "cpu_baseline": cpu_pre},
             "gpu_launches": 4 * args.steps,
             "clocks": clocks,
-            "cpu_baseline": None,
+            "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

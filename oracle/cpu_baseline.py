@@ -82,3 +82,45 @@ def run_reference_arm(lengths: np.ndarray, geom, steps: int, warmup: int,
             "cores": cores,
             "sample": f"{len(sp['lens'])} requests of one layer per step (seeded); fp32 torch "
                       "eager attention over gathered pages"}
+
+
+def time_prefill_sample(qo_lens: np.ndarray, prefix_lens: np.ndarray, geom,
+                        budget_s: float = 10.0, sample: int = 2, seed: int = 2025) -> dict:
+    """Repeats the oracle's causal prefill of `sample` chunks (seeded choice
+    among the workload's chunks) for about budget_s seconds; TFLOP/s of the
+    visible (unmasked) query-key pairs, 4 * D FLOPs each, as the GPU arm
+    counts them."""
+    cores = _cores()
+    rng = np.random.default_rng(seed)
+    idx = np.sort(rng.choice(len(qo_lens), size=min(sample, len(qo_lens)), replace=False))
+    qo = np.asarray(qo_lens)[idx].astype(np.int64)
+    pre = np.asarray(prefix_lens)[idx].astype(np.int64)
+    kv = qo + pre
+    P = geom.page_size
+    npages = (kv + P - 1) // P
+    kv_indptr = np.zeros(len(kv) + 1, dtype=np.int64)
+    np.cumsum(npages, out=kv_indptr[1:])
+    qo_indptr = np.zeros(len(qo) + 1, dtype=np.int64)
+    np.cumsum(qo, out=qo_indptr[1:])
+    N = int(kv_indptr[-1])
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(N, generator=g).numpy()
+    last = (kv - (npages - 1) * P).astype(np.int64)
+    pool = torch.randn((N, 2, geom.num_kv_heads, P, geom.head_dim), generator=g)
+    pool = pool.to(torch.bfloat16).to(torch.float32)
+    q = torch.randn((int(qo.sum()), geom.num_qo_heads, geom.head_dim), generator=g)
+    q = q.to(torch.bfloat16).to(torch.float32)
+    pairs = float(sum(int(n) * int(p) + int(n) * (int(n) + 1) // 2 for n, p in zip(qo, pre)))
+    flops = 4.0 * geom.head_dim * geom.num_qo_heads * pairs
+    attention.prefill(q, qo_indptr, pool, kv_indptr, perm, last)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        attention.prefill(q, qo_indptr, pool, kv_indptr, perm, last)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return {"value": round(flops * reps / el / 1e12, 5), "unit": "TFLOP/s", "cores": cores,
+            "kind": "port",
+            "sample": f"{len(qo)} of the workload's prefill chunks (seeded), {reps} passes in "
+                      f"{el:.1f} s; fp32 torch eager causal attention over gathered pages"}
