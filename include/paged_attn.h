@@ -205,6 +205,14 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
                        const pa_kv_cache* cache, const int32_t* kv_indices,
                        const int32_t* kv_indptr, int32_t batch_size, void* stream);
 
+/* Diagnostic with no reference counterpart: launches one warp that waits on
+ * a barrier nothing completes, with a limit of limit_cycles SM clocks (at
+ * most the kernels' own limit). The wait gives up, PA_ERR_TIMEOUT lands in
+ * the device status word, the kernel returns and the context stays usable —
+ * the path every bounded wait in this library takes, exercised without a
+ * fault. */
+int pa_selftest_wait_timeout(int64_t limit_cycles, void* stream);
+
 /* Workspace bytes pa_decode_plan needs for this batch geometry. */
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim);

@@ -96,6 +96,7 @@ SIGNATURES = {
          c_void_p, c_void_p, c_int32, c_int32, c_float, c_float, POINTER(PagedKVCache), c_void_p,
          c_void_p, c_int32, c_void_p],
     ),
+    "pa_selftest_wait_timeout": (c_int32, [c_int64, c_void_p]),
     "pa_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "pa_decode_plan": (
         c_int32,

@@ -650,6 +650,12 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
               : go(qkv_rope_append_kernel<__half, 128, 128, 6>, N6::kSmemBytes, &done[7]);
 }
 
+int pa_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > kWaitLimitCycles) return PA_ERR_INVALID_ARGUMENT;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_cycles);
+  return launch_status();
+}
+
 size_t pa_decode_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim) {
   (void)num_qo_heads;

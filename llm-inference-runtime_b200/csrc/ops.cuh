@@ -307,6 +307,22 @@ __global__ void fork_pages_kernel(const ForkParams p) {
   }
 }
 
+// ------------------------------------------------------- wait self-test
+// Exercises the bounded-wait path every kernel relies on, without a fault:
+// one warp waits on an mbarrier that nothing arrives on, with a short limit;
+// the wait gives up, the kernel records PA_ERR_TIMEOUT and returns, and the
+// context stays usable.
+__global__ void wait_selftest_kernel(long long limit_cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const bool ok = mbar_wait_warp_limit(&bar, 0, limit_cycles);
+  if (!ok && threadIdx.x == 0) set_status(PA_ERR_TIMEOUT);
+}
+
 // -------------------------------------------------------------- merge
 // flashinfer.merge_states: v [n, S, H, D], s [n, S, H] (base-2 LSE) ->
 // v_merged [n, H, D], s_merged [n, H]. One warp per (row, head).

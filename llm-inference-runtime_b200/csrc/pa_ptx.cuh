@@ -60,12 +60,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false if
-// the wait ran past kWaitLimitCycles (the caller records a timeout).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// the wait ran past `limit` SM cycles (the caller records a timeout).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          long long limit = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitLimitCycles) return false;
+    if (clock64() - t0 > limit) return false;
   }
   return true;
 }
@@ -74,6 +75,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // by warp-collective instructions (__syncwarp, tcgen05.ld/st .sync.aligned).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+__device__ __forceinline__ bool mbar_wait_warp_limit(uint64_t* bar, uint32_t parity,
+                                                     long long limit) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, limit));
 }
 
 // ---------------------------------------------------------------- TMA

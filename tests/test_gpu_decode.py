@@ -296,3 +296,23 @@ def test_unsupported_options_raise(fi):
         w.plan(t, t[:1], t[:1], 32, 4, 64, 16, logits_soft_cap=30.0)
     with pytest.raises(NotImplementedError):
         w.plan(t, t[:1], t[:1], 32, 4, 64, 16, window_left=128)
+
+
+def test_bounded_wait_times_out_and_context_stays_usable(fi, lir, workloads):
+    """The bounded-wait path without a fault: a kernel waits on a barrier
+    nothing completes, gives up after ~1 ms of SM clocks, reports
+    PA_ERR_TIMEOUT; the next decode on the same context is correct."""
+    torch.cuda.synchronize()
+    lir._lib.device_status()
+    lib = lir._lib.load()
+    assert lib.pa_selftest_wait_timeout(2_000_000, torch.cuda.current_stream().cuda_stream) == 0
+    assert lir._lib.device_status() == lir._lib.PA_ERR_TIMEOUT
+    assert lir._lib.device_status() == 0  # read and cleared
+    geom = workloads.TINYLLAMA
+    prob = workloads.make_decode_problem(geom, 4, 50, 300, seed=21, device=DEV, num_layers=1,
+                                         append=False)
+    got = _decode(fi, prob.q, prob.pool[0], prob.kv_indptr, prob.kv_indices,
+                  prob.kv_last_page_len)
+    want, _ = attention.decode(prob.q, prob.pool[0].float(), prob.kv_indptr, prob.kv_indices,
+                               prob.kv_last_page_len)
+    _check(got, want)
