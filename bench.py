@@ -25,6 +25,8 @@ copied out every layer).
 --impl reference: the reference's attention math on the host cores (the
 CPU oracle: fp32 eager attention over gathered pages), rank 0 only, each
 step a bounded sample of the same workload.
+--impl flashinfer: the same step through FlashInfer itself (the reference's
+GPU path, when the flashinfer package is installed), for comparison.
 """
 
 from __future__ import annotations
@@ -160,14 +162,42 @@ def _global_lengths(batch_total: int, lo: int, hi: int, seed: int = 0) -> np.nda
     return torch.randint(lo, hi + 1, (batch_total,), generator=g).numpy().astype(np.int64) + 1
 
 
+def _backend(args):
+    """The attention module a run drives: this package's FlashInfer-compatible
+    API, or (--impl flashinfer) FlashInfer itself — the reference's GPU path —
+    through the same calls."""
+    if args.impl == "flashinfer":
+        import flashinfer
+        return flashinfer, False
+    lir = importlib.import_module(PKG)
+    lir.build.build()
+    return importlib.import_module(PKG + ".flashinfer_api"), True
+
+
+def _mark_flashinfer(line: dict) -> None:
+    """The --impl flashinfer line: same workload and metric, FlashInfer's kernels."""
+    import flashinfer
+    line["impl"] = "flashinfer"
+    line["flashinfer_version"] = flashinfer.__version__
+    line["gpu_launches"] = 0  # none of this package's kernels run
+    line["roofline"]["kernel"] = "flashinfer BatchDecodeWithPagedKVCacheWrapper"
+    line["roofline"]["traffic"] = None
+    if "prefill" in line:
+        line["prefill"]["roofline"]["kernel"] = "flashinfer BatchPrefillWithPagedKVCacheWrapper"
+
+
+def _check(lir, ours: bool, what: str) -> None:
+    if ours:
+        lir._lib.check_device(what)
+
+
 # ------------------------------------------------------------------ ours
 def run_ours(args):
     rank, world, local = _dist()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lir = importlib.import_module(PKG)
-    lir.build.build()
-    fi = importlib.import_module(PKG + ".flashinfer_api")
+    fi, ours = _backend(args)
     wl, geom, per_gpu, lo, hi, layers, wname = _workload(args)
     P = geom.page_size
 
@@ -219,7 +249,7 @@ def run_ours(args):
     for _ in range(args.warmup):
         step(False)
     torch.cuda.synchronize()
-    lir._lib.check_device("bench warm-up")
+    _check(lir, ours, "bench warm-up")
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -258,7 +288,7 @@ def run_ours(args):
     total_bytes = _sum_over_ranks(float(bytes_step) * args.steps, world)
     value = total_bytes / (ms * 1e-3) / 1e9
     tok_s = _sum_over_ranks(float(B) * args.steps, world) / (ms * 1e-3)
-    lir._lib.check_device("bench timed region")
+    _check(lir, ours, "bench timed region")
 
     # ---- end to end through the public API from pinned host memory
     # Every step copies its inputs in (tables once, then each layer's q and new
@@ -348,12 +378,12 @@ def run_ours(args):
     e2e_ms = _max_over_ranks(t0.elapsed_time(t1), world)
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     ok = torch.equal(h_out[layers - 1], out.cpu())  # same q, same pool state: same result
-    lir._lib.check_device("bench e2e")
+    _check(lir, ours, "bench e2e")
 
     peak, peak_kind = _peaks()
     achieved = bytes_decode / (dec_ms * 1e-3) / 1e9
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and ours:
         cpu = cpu_baseline(prob_lengths=prob.lengths, geom=geom, layers=layers)
     _barrier(world)
     if rank == 0:
@@ -385,7 +415,7 @@ def run_ours(args):
                          "peak_kind": peak_kind, "kernel": "decode_kernel",
                          "bytes_per_launch": bytes_decode,
                          "avg_launch_ms": round(dec_ms, 5),
-                         "traffic": _traffic_from_profile(bytes_decode)},
+                         "traffic": _traffic_from_profile(bytes_decode) if ours else None},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
                     "copies": "pinned host buffers, two copy streams overlapped with compute",
@@ -394,6 +424,8 @@ def run_ours(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if not ours:
+            _mark_flashinfer(line)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -424,8 +456,7 @@ def run_mixed(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lir = importlib.import_module(PKG)
-    lir.build.build()
-    fi = importlib.import_module(PKG + ".flashinfer_api")
+    fi, ours = _backend(args)
     wl, geom, n_dec, lo, hi, layers, wname = _workload(args)
     pre = wl.config3_prefill(seed=rank, device=dev)
     dec = wl.make_decode_problem(geom, n_dec, lo, hi, seed=100 + rank, device=dev, num_layers=1,
@@ -444,8 +475,11 @@ def run_mixed(args):
     ev = []
 
     def step(record):
+        # total_qo (this package's extension) lets the prefill plan run on the
+        # device without reading qo_indptr back; FlashInfer plans on the host
+        extra = {"total_qo": q_pre.shape[0]} if ours else {}
         pw.plan(qo, kvp, kvi, last, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim, 16,
-                causal=True, q_data_type=q_pre.dtype, total_qo=q_pre.shape[0])
+                causal=True, q_data_type=q_pre.dtype, **extra)
         dw.plan(dindptr, dindices, dlast, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim,
                 16, q_data_type=q_dec.dtype)
         e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
@@ -462,7 +496,7 @@ def run_mixed(args):
     for _ in range(args.warmup):
         step(False)
     torch.cuda.synchronize()
-    lir._lib.check_device("bench cfg3 warm-up")
+    _check(lir, ours, "bench cfg3 warm-up")
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
@@ -480,7 +514,7 @@ def run_mixed(args):
     ms = _max_over_ranks(t0.elapsed_time(t1), world)
     pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
-    lir._lib.check_device("bench cfg3")
+    _check(lir, ours, "bench cfg3")
     total_dbytes = _sum_over_ranks(float(dbytes) * args.steps, world)
     value = total_dbytes / (ms * 1e-3) / 1e9
     peak_bw, bw_kind = _peaks()
@@ -489,7 +523,7 @@ def run_mixed(args):
     pre_tf = flops / (pre_ms * 1e-3) / 1e12
     dec_gbs = dbytes / (dec_ms * 1e-3) / 1e9
     cpu, cpu_pre = None, None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and ours:
         from oracle import cpu_baseline as cb
         cpu = cb.time_decode_sample(dec.lengths, geom, budget_s=8.0, sample=16)
         cpu_pre = cb.time_prefill_sample(pre.qo_lens, pre.prefix_lens, geom, budget_s=8.0)
@@ -524,6 +558,8 @@ def run_mixed(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if not ours:
+            _mark_flashinfer(line)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -579,7 +615,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "flashinfer"], default="ours")
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
                     default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -316,3 +316,18 @@ def test_bounded_wait_times_out_and_context_stays_usable(fi, lir, workloads):
     want, _ = attention.decode(prob.q, prob.pool[0].float(), prob.kv_indptr, prob.kv_indices,
                                prob.kv_last_page_len)
     _check(got, want)
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(8, 8, 128), (16, 8, 64), (32, 2, 128), (64, 4, 64),
+                                      (16, 16, 64), (32, 16, 128)])
+def test_decode_every_gqa_group_and_head_block(fi, workloads, hq, hkv, d):
+    """Group sizes 1..16 and kv-head counts above 8 (two head blocks per
+    page): the head-block split of the stream and the GQA rows of the MMA."""
+    geom = workloads.Geometry(num_qo_heads=hq, num_kv_heads=hkv, head_dim=d)
+    prob = workloads.make_decode_problem(geom, 9, 1, 1500, seed=hq * 7 + hkv, num_layers=1)
+    got, lse = _decode(fi, prob.q, prob.pool[0], prob.kv_indptr, prob.kv_indices,
+                       prob.kv_last_page_len, return_lse=True)
+    want, want_lse = attention.decode(prob.q, prob.pool[0].float(), prob.kv_indptr,
+                                      prob.kv_indices, prob.kv_last_page_len)
+    _check(got, want)
+    assert torch.allclose(lse.cpu(), want_lse, atol=2e-3, rtol=1e-4)

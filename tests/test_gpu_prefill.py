@@ -154,3 +154,17 @@ def test_prefill_rejects_chunk_longer_than_cache(fi, lir, workloads):
         assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
     finally:
         fa._CHECK = saved
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(8, 8, 128), (16, 8, 64), (32, 2, 128), (64, 4, 64),
+                                      (16, 16, 64)])
+def test_every_gqa_group_size(fi, workloads, hq, hkv, d):
+    """GQA packing for group sizes 1, 2, 16 (8 and 4 are the model configs):
+    rows per tile = 128 / g queries x g heads."""
+    geom = workloads.Geometry(num_qo_heads=hq, num_kv_heads=hkv, head_dim=d)
+    prob = _problem(workloads, geom, [70, 1, 200], [33, 0, 500], seed=40 + hq + hkv)
+    got, lse = _prefill(fi, prob.q, prob.pool[0], prob.qo_indptr, prob.kv_indptr,
+                        prob.kv_indices, prob.kv_last_page_len, return_lse=True)
+    want, want_lse = _oracle(prob)
+    _check(got, want)
+    assert torch.allclose(lse.cpu(), want_lse, atol=2e-3, rtol=1e-4)
