@@ -238,6 +238,28 @@ int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const p
                   float sm_scale, void* workspace, size_t workspace_bytes, void* out, float* lse,
                   void* stream);
 
+/* Replaces the reference's decode-step pair (src/models/llama.py:188-210 then
+ * 230-245, with the batch indices / positions step_executor.py:204-225
+ * builds for decode: one new token per request, batch_indices = arange(B))
+ *   flashinfer.append_paged_kv_cache(k, v, arange(B), positions, cache, ...)
+ *   BatchDecodeWithPagedKVCacheWrapper.forward(q, cache)
+ * with one launch. Row b of append_key / append_value [B, H_kv, D] (strides
+ * in elements, last dim contiguous) goes to position positions[b] of request
+ * b's pages exactly as pa_append_paged_kv_cache places it (bit-identical pool,
+ * same device checks), and the attention sees it as if the append had run
+ * first: the output equals pa_append_paged_kv_cache followed by
+ * pa_decode_run. The other arguments mean what they mean for pa_decode_run;
+ * the same plan serves both. */
+int pa_decode_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                         const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
+                         const void* append_value, int64_t value_stride_n,
+                         int64_t value_stride_h, const int32_t* positions,
+                         const pa_kv_cache* cache, const int32_t* kv_indices,
+                         const int32_t* kv_indptr, const int32_t* kv_last_page_len,
+                         int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+                         void* workspace, size_t workspace_bytes, void* out, float* lse,
+                         void* stream);
+
 /* Workspace bytes pa_prefill_plan needs. */
 size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int32_t num_qo_heads,
                                   int32_t num_kv_heads, int32_t head_dim);

@@ -691,11 +691,24 @@ int pa_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, in
                       sh.g.hb, /*min_per_group=*/4, static_cast<uint8_t*>(workspace));
 }
 
-int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
-                  const int32_t* kv_indices, const int32_t* kv_indptr,
-                  const int32_t* kv_last_page_len, int32_t batch_size, int32_t num_qo_heads,
-                  float sm_scale, void* workspace, size_t workspace_bytes, void* out, float* lse,
-                  void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Decode-step append rows handed to decode_run (nullptr: plain decode).
+struct DecodeAppend {
+  const void* key;
+  int64_t key_stride_n, key_stride_h;
+  const void* value;
+  int64_t value_stride_n, value_stride_h;
+  const int32_t* positions;
+};
+
+int decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+               const int32_t* kv_indices, const int32_t* kv_indptr,
+               const int32_t* kv_last_page_len, int32_t batch_size, int32_t num_qo_heads,
+               float sm_scale, void* workspace, size_t workspace_bytes, void* out, float* lse,
+               void* stream, const DecodeAppend* app) {
   int st = check_cache(cache);
   if (st != PA_OK) return st;
   if (q == nullptr || out == nullptr || kv_indices == nullptr || kv_indptr == nullptr ||
@@ -747,12 +760,69 @@ int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const p
   p.counter = reinterpret_cast<int32_t*>(ws + L.counter);
   p.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
   p.part_o = reinterpret_cast<float*>(ws + L.part_o);
+  p.append_pos = nullptr;
+  p.new_k = p.new_v = nullptr;
+  p.new_k_stride_n = p.new_k_stride_h = p.new_v_stride_n = p.new_v_stride_h = 0;
+  p.k_pool = p.v_pool = nullptr;
+  p.pool_page_stride = p.pool_head_stride = p.pool_token_stride = 0;
+  if (app != nullptr) {
+    const int esz = 2;  // bf16 / fp16
+    p.append_pos = app->positions;
+    p.new_k = static_cast<const uint8_t*>(app->key);
+    p.new_v = static_cast<const uint8_t*>(app->value);
+    p.new_k_stride_n = app->key_stride_n * esz;
+    p.new_k_stride_h = app->key_stride_h * esz;
+    p.new_v_stride_n = app->value_stride_n * esz;
+    p.new_v_stride_h = app->value_stride_h * esz;
+    // the descriptor's bases are const for the read-only entry points; the
+    // append writes through them as pa_append_paged_kv_cache does
+    p.k_pool = const_cast<uint8_t*>(static_cast<const uint8_t*>(cache->k_base));
+    p.v_pool = const_cast<uint8_t*>(static_cast<const uint8_t*>(cache->v_base));
+    p.pool_page_stride = cache->page_stride * esz;
+    p.pool_head_stride = cache->head_stride * esz;
+    p.pool_token_stride = cache->token_stride * esz;
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cache->dtype == PA_DTYPE_BF16)
     return D == 64 ? launch_decode<__nv_bfloat16, 64>(km, vm, p, sh, dev, s)
                    : launch_decode<__nv_bfloat16, 128>(km, vm, p, sh, dev, s);
   return D == 64 ? launch_decode<__half, 64>(km, vm, p, sh, dev, s)
                  : launch_decode<__half, 128>(km, vm, p, sh, dev, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int pa_decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                  const int32_t* kv_indices, const int32_t* kv_indptr,
+                  const int32_t* kv_last_page_len, int32_t batch_size, int32_t num_qo_heads,
+                  float sm_scale, void* workspace, size_t workspace_bytes, void* out, float* lse,
+                  void* stream) {
+  return decode_run(q, q_stride_n, q_stride_h, cache, kv_indices, kv_indptr, kv_last_page_len,
+                    batch_size, num_qo_heads, sm_scale, workspace, workspace_bytes, out, lse,
+                    stream, nullptr);
+}
+
+int pa_decode_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                         const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
+                         const void* append_value, int64_t value_stride_n,
+                         int64_t value_stride_h, const int32_t* positions,
+                         const pa_kv_cache* cache, const int32_t* kv_indices,
+                         const int32_t* kv_indptr, const int32_t* kv_last_page_len,
+                         int32_t batch_size, int32_t num_qo_heads, float sm_scale,
+                         void* workspace, size_t workspace_bytes, void* out, float* lse,
+                         void* stream) {
+  if (append_key == nullptr || append_value == nullptr || positions == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(append_key) || !aligned16(append_value) || key_stride_n % 8 ||
+      key_stride_h % 8 || value_stride_n % 8 || value_stride_h % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  const DecodeAppend app{append_key, key_stride_n, key_stride_h, append_value,
+                         value_stride_n, value_stride_h, positions};
+  return decode_run(q, q_stride_n, q_stride_h, cache, kv_indices, kv_indptr, kv_last_page_len,
+                    batch_size, num_qo_heads, sm_scale, workspace, workspace_bytes, out, lse,
+                    stream, &app);
 }
 
 int pa_merge_states(const void* v, const float* s, int32_t seq_len, int32_t num_states,

@@ -28,6 +28,10 @@
 //   * A (request, kv head) segment that straddles runs is written as
 //     normalised fp32 partials plus base-2 LSE; the last warp to finish that
 //     segment (atomic counter per segment) merges the pieces in the same launch.
+//   * Decode-step append (optional): the warp that loads the page holding a
+//     request's new token writes that token's K / V row of its head into the
+//     pool and over the stale row of the loaded stage, so the step's append
+//     costs no launch and no extra read of the page.
 #pragma once
 
 #include "pa_common.cuh"
@@ -283,9 +287,11 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   const int hq = p.num_qo_heads;
   T* out = reinterpret_cast<T*>(p.out);
 
-  // Requests without pages produce zeros (and LSE = -inf).
+  // Requests without pages produce zeros (and LSE = -inf); none can take an
+  // appended token.
   for (int e = gw; e < hdr->num_empty; e += total_warps) {
     const int b = p.empty[e];
+    if (p.append_pos != nullptr && lane == 0) set_status(PA_ERR_DEVICE_CHECK);
     for (int i = lane; i < hq * D / 8; i += 32)
       reinterpret_cast<uint4*>(out + static_cast<size_t>(b) * hq * D)[i] = make_uint4(0, 0, 0, 0);
     if (p.lse != nullptr)
@@ -358,7 +364,7 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   uint32_t qf[KS][4];
   float o[NT][4];
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  int seg_start = 0, last_len = kPage, head = 0;
+  int seg_start = 0, last_len = kPage, head = 0, apos = -1;
   const bool row0 = gid < G, row1 = gid + 8 < G;
   // Row of token r of this warp's head inside a panel of the stage.
   const int row_mul = p.heads_inner ? HB : 1;
@@ -393,6 +399,15 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
       l0 = l1 = 0.f;
       seg_start = NHB * cc.base + cc.hblk * cc.n;
       last_len = __ldg(p.kv_last_page_len + cc.b);
+      if (p.append_pos != nullptr) {
+        // the same rule as pa_append_paged_kv_cache: the position must fall
+        // inside the request's pages
+        apos = __ldg(p.append_pos + cc.b);
+        if (apos < 0 || apos / kPage >= cc.n) {
+          if (lane == 0) set_status(PA_ERR_DEVICE_CHECK);
+          apos = -1;
+        }
+      }
     }
 
     if (!mbar_wait(&bars[stage], phase)) {
@@ -403,6 +418,29 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
     const uint32_t kb = smem_u32(kst);
     const uint32_t vb = kb + PANELS * panel_bytes;
     const int valid = (cc.j == cc.n - 1) ? last_len : kPage;
+
+    // ---- decode-step append: this page holds the request's new token
+    if (apos >= 0 && cc.j == apos / kPage) {
+      constexpr int CH = D / 8;  // 16-byte chunks per row: lanes [0, CH) K, [CH, 2 CH) V
+      const int slot = apos % kPage;
+      const int page = __ldg(p.kv_indices + cc.base + cc.j);
+      if (lane < 2 * CH) {
+        const int kv = lane / CH, c = lane - kv * CH;
+        const uint8_t* src = kv ? p.new_v + cc.b * p.new_v_stride_n + head * p.new_v_stride_h
+                                : p.new_k + cc.b * p.new_k_stride_n + head * p.new_k_stride_h;
+        const uint4 val = __ldg(reinterpret_cast<const uint4*>(src) + c);
+        if (page >= 0 && page < p.num_pages) {
+          uint8_t* dst = (kv ? p.v_pool : p.k_pool) + page * p.pool_page_stride +
+                         head * p.pool_head_stride + slot * p.pool_token_stride;
+          reinterpret_cast<uint4*>(dst)[c] = val;
+        }
+        // the loaded stage still holds the slot's old bytes
+        *reinterpret_cast<uint4*>(kst + (kv * PANELS + (c >> 3)) * panel_bytes +
+                                  sw128(slot * row_mul + row_add, c & 7)) = val;
+        fence_proxy_async();  // before the stage is refilled by TMA
+      }
+      __syncwarp();
+    }
 
     // ---- S = Q K^T over the 16 keys of this page
     float s[2][4];

@@ -95,6 +95,16 @@ struct DecodeParams {
   int32_t* counter;
   float* part_lse;
   float* part_o;
+  // Optional decode-step append (pa_decode_append_run): request b's new K / V
+  // row (row b of new_k / new_v) goes to position append_pos[b] of its pages
+  // before the attention reads that page. append_pos == nullptr: no append.
+  const int32_t* append_pos;
+  const uint8_t* new_k;
+  const uint8_t* new_v;
+  int64_t new_k_stride_n, new_k_stride_h, new_v_stride_n, new_v_stride_h;  // bytes
+  uint8_t* k_pool;
+  uint8_t* v_pool;
+  int64_t pool_page_stride, pool_head_stride, pool_token_stride;  // bytes
 };
 
 }  // namespace pa

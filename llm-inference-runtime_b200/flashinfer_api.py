@@ -328,6 +328,33 @@ class BatchDecodeWithPagedKVCacheWrapper:
     def run(self, q: torch.Tensor, paged_kv_cache, *args, q_scale=None, k_scale=None,
             v_scale=None, out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
             return_lse: bool = False, **kwargs):
+        return self._run(q, paged_kv_cache, None, q_scale, k_scale, v_scale, out, lse,
+                         return_lse)
+
+    def run_with_append(self, q: torch.Tensor, paged_kv_cache, append_key: torch.Tensor,
+                        append_value: torch.Tensor, positions: torch.Tensor, *,
+                        out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                        return_lse: bool = False):
+        """This package's extension: the decode step's
+        ``append_paged_kv_cache(append_key, append_value, arange(B), positions, ...)``
+        followed by :meth:`run`, as one launch (row b of append_key /
+        append_value is request b's new token). The pool afterwards is
+        bit-identical to the two-call sequence and so is the output."""
+        desc = kv_cache_desc(paged_kv_cache, self._kv_layout)
+        if append_key.dtype != append_value.dtype or _dtype_code(append_key.dtype) != desc.dtype:
+            raise ValueError("append_key / append_value must have the KV cache's dtype")
+        for name, x in (("append_key", append_key), ("append_value", append_value)):
+            _row_strides(x, name)
+            if tuple(x.shape) != (self._batch, desc.num_kv_heads, desc.head_dim):
+                raise ValueError(f"{name} must be [{self._batch}, {desc.num_kv_heads}, "
+                                 f"{desc.head_dim}]")
+        positions = _i32_on(positions, q.device, "positions")
+        if positions.numel() != self._batch:
+            raise ValueError("positions must hold one entry per request")
+        return self._run(q, paged_kv_cache, (append_key, append_value, positions), None, None,
+                         None, out, lse, return_lse)
+
+    def _run(self, q, paged_kv_cache, append, q_scale, k_scale, v_scale, out, lse, return_lse):
         if not self._planned:
             raise RuntimeError("plan() must be called before run()")
         desc = kv_cache_desc(paged_kv_cache, self._kv_layout)
@@ -346,12 +373,23 @@ class BatchDecodeWithPagedKVCacheWrapper:
             lse = torch.empty((self._batch, self._hq), dtype=torch.float32, device=q.device)
         scale = self._sm_scale if self._sm_scale is not None else 1.0 / math.sqrt(self._d)
         scale *= _check_scales(q_scale, k_scale, v_scale)
-        _lib.check(_lib.load().pa_decode_run(
-            _p(q), qsn, qsh, ctypes.byref(desc), _p(self._indices), _p(self._indptr),
-            _p(self._last), self._batch, self._hq, float(scale), _p(self._ws),
-            self._ws.numel() * self._ws.element_size(), _p(out), _p(lse), _stream()),
-            "BatchDecodeWithPagedKVCacheWrapper.run")
-        _after("BatchDecodeWithPagedKVCacheWrapper.run")
+        ws_bytes = self._ws.numel() * self._ws.element_size()
+        if append is None:
+            _lib.check(_lib.load().pa_decode_run(
+                _p(q), qsn, qsh, ctypes.byref(desc), _p(self._indices), _p(self._indptr),
+                _p(self._last), self._batch, self._hq, float(scale), _p(self._ws), ws_bytes,
+                _p(out), _p(lse), _stream()), "BatchDecodeWithPagedKVCacheWrapper.run")
+            _after("BatchDecodeWithPagedKVCacheWrapper.run")
+        else:
+            k, v, pos = append
+            ksn, ksh = k.stride(0), k.stride(1)
+            vsn, vsh = v.stride(0), v.stride(1)
+            _lib.check(_lib.load().pa_decode_append_run(
+                _p(q), qsn, qsh, _p(k), ksn, ksh, _p(v), vsn, vsh, _p(pos), ctypes.byref(desc),
+                _p(self._indices), _p(self._indptr), _p(self._last), self._batch, self._hq,
+                float(scale), _p(self._ws), ws_bytes, _p(out), _p(lse), _stream()),
+                "BatchDecodeWithPagedKVCacheWrapper.run_with_append")
+            _after("BatchDecodeWithPagedKVCacheWrapper.run_with_append")
         return (out, lse) if return_lse else out
 
     def forward(self, q: torch.Tensor, paged_kv_cache, pos_encoding_mode: str = "NONE",
