@@ -153,3 +153,29 @@ def test_fused_append_rejects_bad_rows(fi, workloads):
         w.run_with_append(prob.q.to(DEV), pool, k.half(), k.half(), _t(prob.positions))
     with pytest.raises(ValueError):
         w.run_with_append(prob.q.to(DEV), pool, k, k, _t(prob.positions[:2]))
+
+
+def test_full_size_config2_layer_fused(fi, workloads):
+    """Configuration 2 size, one layer (B=256, L~U[1024,4096]) through the fused
+    call the bench times: pool rows bit-exact against the two-call sequence,
+    outputs bit-identical, oracle on a sample of requests."""
+    prob = workloads.make_decode_problem(workloads.TINYLLAMA, 256, 1024, 4096, seed=0,
+                                         device=DEV, num_layers=1)
+    indptr, indices, last = prob.device_tables(DEV)
+    pos = _t(prob.positions)
+    w = fi.BatchDecodeWithPagedKVCacheWrapper(torch.empty(128 << 20, dtype=torch.uint8,
+                                                          device=DEV), "HND")
+    w.plan(indptr, indices, last, 32, 4, 64, 16, q_data_type=torch.bfloat16)
+    pool_a = prob.pool[0].clone()
+    fi.append_paged_kv_cache(prob.k_new, prob.v_new, _t(np.arange(256)), pos, pool_a, indices,
+                             indptr, last, kv_layout="HND")
+    out_a = w.run(prob.q, pool_a)
+    pool_b = prob.pool[0]
+    out_b = w.run_with_append(prob.q, pool_b, prob.k_new, prob.v_new, pos)
+    assert torch.equal(pool_a, pool_b)
+    assert torch.equal(out_a, out_b)
+    sample = [0, 1, 77, 128, 200, 255]
+    want, _ = attention.decode(prob.q.cpu(), pool_b.cpu(), prob.kv_indptr, prob.kv_indices,
+                               prob.kv_last_page_len, requests=sample)
+    mx, mean, ok = attention.compare(out_b.cpu()[sample], want[sample], MAX_ABS, MEAN_ABS)
+    assert ok, f"max-abs {mx:.3e} mean-abs {mean:.3e}"
