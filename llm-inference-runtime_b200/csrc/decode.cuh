@@ -211,19 +211,35 @@ __device__ __noinline__ void merge_segment(const float* part_lse, const float* p
     const int r = it / C4, c = (it - r * C4) * 4;
     float m = -INFINITY, w = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int u = u0; u <= u1; ++u) {
-      const size_t sl = static_cast<size_t>((u * 2 + (seg_start <= u * Q ? 0 : 1)) * HB + hh);
-      const float l = __ldcg(part_lse + sl * kMaxGroup + r);
-      const float4 v =
-          __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
-      const float mn = fmaxf(m, l);
-      const float sc = ex2(m - mn), wt = ex2(l - mn);
-      acc.x = acc.x * sc + wt * v.x;
-      acc.y = acc.y * sc + wt * v.y;
-      acc.z = acc.z * sc + wt * v.z;
-      acc.w = acc.w * sc + wt * v.w;
-      w = w * sc + wt;
-      m = mn;
+    // pieces in batches of 4: all loads of a batch are in flight together,
+    // so a segment of n pieces costs ceil(n / 4) L2 round trips
+    constexpr int kBatch = 4;
+    for (int u = u0; u <= u1; u += kBatch) {
+      float lb[kBatch];
+      float4 vb[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        lb[k] = -INFINITY;
+        vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (u + k <= u1) {
+          const int uk = u + k;
+          const size_t sl = static_cast<size_t>((uk * 2 + (seg_start <= uk * Q ? 0 : 1)) * HB + hh);
+          lb[k] = __ldcg(part_lse + sl * kMaxGroup + r);
+          vb[k] = __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        if (u + k > u1) break;
+        const float mn = fmaxf(m, lb[k]);
+        const float sc = ex2(m - mn), wt = ex2(lb[k] - mn);
+        acc.x = acc.x * sc + wt * vb[k].x;
+        acc.y = acc.y * sc + wt * vb[k].y;
+        acc.z = acc.z * sc + wt * vb[k].z;
+        acc.w = acc.w * sc + wt * vb[k].w;
+        w = w * sc + wt;
+        m = mn;
+      }
     }
     const float inv = 1.f / w;
     uint2 packed;
