@@ -19,7 +19,12 @@ no data-path collective (gloo is used only for the barrier and the max over
 ranks of the timed region).
 
 value = algorithmic bytes of all ranks (every K/V element read once, q read,
-o written, appended rows read + written) / max-over-ranks device time.
+o written, appended rows read + written) / max-over-ranks device time of
+the step replayed from a CUDA graph (captured once after warm-up; --eager
+times eager launches instead). The same steps are also timed with eager
+launches first: the per-launch events of that loop give the decode kernel's
+duration for the roofline, and its step time is reported as
+eager_ms_per_step.
 e2e = the same bytes / device time of the same step driven through the
 public API from pinned host buffers (tables, q, new K/V copied in; outputs
 copied out every layer).
@@ -273,25 +278,46 @@ def run_ours(args):
                  if "unique_pages" in prob.extra else bytes_decode)
     small = unique_kv < (100 << 20)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if small else None
-    if small:
-        ms_local = 0.0
-        for _ in range(args.steps):
-            flush.view(torch.int64).sum()
-            t0.record(stream)
-            step(True)
-            t1.record(stream)
-            torch.cuda.synchronize()
-            ms_local += t0.elapsed_time(t1)
-    else:
+
+    def timed(run_step) -> float:
+        if small:
+            total = 0.0
+            for _ in range(args.steps):
+                flush.view(torch.int64).sum()
+                t0.record(stream)
+                run_step()
+                t1.record(stream)
+                torch.cuda.synchronize()
+                total += t0.elapsed_time(t1)
+            return total
         t0.record(stream)
         for _ in range(args.steps):
-            step(True)
+            run_step()
         t1.record(stream)
         torch.cuda.synchronize()
-        ms_local = t0.elapsed_time(t1)
+        return t0.elapsed_time(t1)
+
+    # Eager launches (the per-launch events give the decode kernel's duration
+    # for the roofline), then -- this package only -- the same step captured
+    # once in a CUDA graph and replayed, which is how a serving loop runs a
+    # launch-bound decode step. FlashInfer's plan works on the host and cannot
+    # be captured, so its arm stays eager.
+    eager_local = timed(lambda: step(True))
+    graph = None
+    if ours and not args.eager:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(False)
+        graph.replay()
+        torch.cuda.synchronize()
+        _barrier(world)
+        ms_local = timed(graph.replay)
+    else:
+        ms_local = eager_local
     _barrier(world)
     clocks = sampler.stop()
     ms = _max_over_ranks(ms_local, world)
+    eager_ms = _max_over_ranks(eager_local, world)
     dec_ms = statistics.mean(a.elapsed_time(b) for a, b in dec_events)
     total_bytes = _sum_over_ranks(float(bytes_step) * args.steps, world)
     value = total_bytes / (ms * 1e-3) / 1e9
@@ -406,6 +432,8 @@ def run_ours(args):
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) q/K/V, random page permutation, random-init",
+            "step_launch": "CUDA graph replay" if graph is not None else "eager",
+            "eager_ms_per_step": round(eager_ms / args.steps, 4),
             "config": {"workload": wname, "layers": layers,
                        "num_qo_heads": geom.num_qo_heads, "num_kv_heads": geom.num_kv_heads,
                        "head_dim": geom.head_dim, "page_size": P,
@@ -677,6 +705,8 @@ def main():
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
                     default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the decode step with eager launches instead of a CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
