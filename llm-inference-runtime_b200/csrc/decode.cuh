@@ -19,8 +19,10 @@
 //     every group moves the same bytes however skewed the context lengths are
 //     (split-KV with no host-side plan).
 //   * A stage is refilled by whichever warp of the group releases it last
-//     (shared-memory arrival counter), with a page id loaded one refill ahead.
-//     No warp ever blocks on another warp's progress.
+//     (shared-memory arrival counter). With one head block per page the run
+//     is a contiguous slice of kv_indices, read 32 page ids per load a chunk
+//     ahead; otherwise a cursor loads each page id one refill ahead. No warp
+//     ever blocks on another warp's progress.
 //   * The g query heads of a kv head are the rows of one m16n8k16 tile, so a
 //     loaded page is shared by the whole GQA group: S = Q K^T (mma.sync, fp32
 //     accumulate), online softmax on the S fragments in registers (quad
@@ -353,20 +355,38 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   // positions (one page-id round trip, lane-parallel); warp 0 of the group
   // fills the ring. Position S, if any, is the first refill: its id is kept
   // in pf_page so each refill issues with an id loaded one iteration early.
+  //
+  // With one head block per page (H_kv <= 8) run position k is simply
+  // kv_indices[s0 + k]: the page ids are then read lane-parallel, 32 per
+  // load (chunk c of the run: position 32 c + lane), one chunk ahead of the
+  // refills that use them, so no dependent global load sits between two
+  // refills. pg_a holds chunk ca, pg_b chunk ca + 1.
+  const bool flat = NHB == 1;
+  auto chunk_ids = [&](int c) {
+    const int k = 32 * c + lane;
+    return k < cnt ? __ldg(p.kv_indices + s0 + k) : 0;
+  };
+  int pg_a = 0, pg_b = 0, ca = 0;
   const int npro = min(S, cnt);
   const int nwalk = min(S + 1, cnt);
-  if (lane == 0) {
-    for (int k = 0; k < nwalk; ++k) {
-      if (k > 0) cursor_next(pc, p.kv_indptr, NHB);
-      walk[k] = pc.base + pc.j;
-      walk[S + 1 + k] = pc.hblk;
-    }
-  }
-  __syncwarp();
   int my_page = 0, my_hb = 0;
-  if (lane < nwalk) {
-    my_page = __ldg(p.kv_indices + walk[lane]);
-    my_hb = walk[S + 1 + lane];
+  if (flat) {
+    pg_a = chunk_ids(0);
+    pg_b = chunk_ids(1);
+    my_page = pg_a;  // positions 0 .. S < 32 are all in chunk 0
+  } else {
+    if (lane == 0) {
+      for (int k = 0; k < nwalk; ++k) {
+        if (k > 0) cursor_next(pc, p.kv_indptr, NHB);
+        walk[k] = pc.base + pc.j;
+        walk[S + 1 + k] = pc.hblk;
+      }
+    }
+    __syncwarp();
+    if (lane < nwalk) {
+      my_page = __ldg(p.kv_indices + walk[lane]);
+      my_hb = walk[S + 1 + lane];
+    }
   }
   int pf_page = __shfl_sync(0xffffffffu, my_page, npro < cnt ? npro : 0);
   int pf_hb = __shfl_sync(0xffffffffu, my_hb, npro < cnt ? npro : 0);
@@ -550,16 +570,28 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
     __syncwarp();
 
     // Release the stage. The last warp of the group to release it refills it
-    // with the page S positions ahead; every warp then moves its copy of the
-    // refill cursor and loads the next page id (used next iteration).
+    // with the page S positions ahead. Flat runs take that page id from the
+    // chunk registers (every warp keeps its own copy in step); otherwise
+    // every warp moves its copy of the refill cursor and loads the next page
+    // id (used next iteration).
+    const int kr = i + S;
+    int rpage = pf_page;
+    if (flat) {
+      if ((kr >> 5) > ca) {
+        pg_a = pg_b;
+        ++ca;
+        pg_b = chunk_ids(ca + 1);
+      }
+      rpage = __shfl_sync(0xffffffffu, pg_a, kr & 31);
+    }
     if (lane == 0) {
       __threadfence_block();
       const int old = atomicAdd(&rel[stage], 1);
-      if ((old + 1) % HB == 0 && i + S < cnt) {
+      if ((old + 1) % HB == 0 && kr < cnt) {
         __threadfence_block();
-        issue(stage, pf_page, pf_hb);
+        issue(stage, rpage, flat ? 0 : pf_hb);
       }
-      if (i + S + 1 < cnt) {
+      if (!flat && kr + 1 < cnt) {
         cursor_next(pc, p.kv_indptr, NHB);
         pf_page = __ldg(p.kv_indices + pc.base + pc.j);
         pf_hb = pc.hblk;
