@@ -21,8 +21,8 @@
 //     It never waits on shared memory between MMAs (the tensor pipe queues
 //     only a couple of MMAs, so any such wait would idle it): its hand-offs
 //     are named barriers.
-//   * warp 10 — relay: waits for each K / V tile's TMA completion and meets
-//     the issuer on a named barrier.
+//   * warps 10 / 11 — relays: wait for each K (warp 10) or V (warp 11) tile's
+//     TMA completion and meet the issuer on that tile's named barrier.
 //   * warps 0-3 / 4-7 — softmax + epilogue of Q tile 0 / 1, one thread per
 //     row (= TMEM lane): causal / length mask, online softmax in base 2 with
 //     lazy O rescaling (only when a row's max grows by more than 2^8), P back
@@ -75,15 +75,16 @@ __device__ __forceinline__ uint32_t pack_p<__half>(float lo, float hi) {
 constexpr int kPfRows = 128;  // query rows per tile (MMA M)
 constexpr int kPfKeys = 128;  // keys per K/V tile (MMA N of S, K of PV): 8 pages
 // Warpgroups 0 / 1 (warps 0-3 / 4-7): softmax + epilogue of Q tile 0 / 1.
-// Warpgroup 2: warp 8 TMA producer, warp 9 tcgen05 issuer, warp 10 relays
-// TMA completions to the issuer, warp 11 idle.
+// Warpgroup 2: warp 8 TMA producer, warp 9 tcgen05 issuer, warps 10 / 11
+// relay K / V TMA completions to the issuer.
 // Launched at 168 registers per thread (384 x 168 = 64512 of 65536); after
 // setup warpgroup 2 drops to 56 and warpgroups 0-1 rise to 224:
 // 2 x 128 x 224 + 128 x 56 = 64512, exactly the launch total.
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
-constexpr int kPfRelayWarp = 10;
+constexpr int kPfRelayWarp = 10;   // K tiles
+constexpr int kPfRelayVWarp = 11;  // V tiles
 // Named barriers (0 is __syncthreads): P_t written (softmax warpgroup t ->
 // issuer warp), K / V tile landed (relay warp -> issuer warp).
 constexpr int kPfBarP = 1;  // + t
@@ -458,24 +459,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (!mbar_wait_warp(mma_done, 0)) failed = true;
       if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
     }
-  } else if (warp == kPfRelayWarp) {
+  } else if (warp == kPfRelayWarp || warp == kPfRelayVWarp) {
     regs_dec<kPfRegsOther>();
-    // ------------------------------------------------------------ relay
-    // Waits for each K / V tile's TMA completion and meets the issuer on a
-    // named barrier, in the order the issuer needs them (K_0, V_0, K_1, ...).
-    // After a timeout it keeps meeting the issuer so no barrier is left
+    // ------------------------------------------------------------ relays
+    // Each waits for its tiles' TMA completions (warp 10: K, warp 11: V) and
+    // meets the issuer on that tile's named barrier. Separate warps, so a V
+    // tile landing late never holds back the hand-off of the next K tile.
+    // After a timeout a relay keeps meeting the issuer so no barrier is left
     // short of arrivals.
+    const bool is_k = warp == kPfRelayWarp;
+    uint64_t* full = is_k ? k_full : v_full;
+    const int bar = is_k ? kPfBarK : kPfBarV;
     bool rfail = false;
     for (int j = 0; j < ntiles; ++j) {
-      const int st = j % S;
-      if (!rfail && !mbar_wait_warp(&k_full[st], (j / S) & 1)) rfail = true;
-      named_bar_sync(kPfBarK, kPfBarKVThreads);
-      if (!rfail && !mbar_wait_warp(&v_full[st], (j / S) & 1)) rfail = true;
-      named_bar_sync(kPfBarV, kPfBarKVThreads);
+      if (!rfail && !mbar_wait_warp(&full[j % S], (j / S) & 1)) rfail = true;
+      named_bar_sync(bar, kPfBarKVThreads);
     }
     if (rfail && lane == 0) set_status(PA_ERR_TIMEOUT);
-  } else if (warp > kPfRelayWarp) {
-    regs_dec<kPfRegsOther>();
   } else {
     regs_inc<kPfRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
