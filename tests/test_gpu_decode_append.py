@@ -179,3 +179,31 @@ def test_full_size_config2_layer_fused(fi, workloads):
                                prob.kv_last_page_len, requests=sample)
     mx, mean, ok = attention.compare(out_b.cpu()[sample], want[sample], MAX_ABS, MEAN_ABS)
     assert ok, f"max-abs {mx:.3e} mean-abs {mean:.3e}"
+
+
+def test_full_size_config5_sampled(fi, workloads):
+    """Configuration 5 at full size on one GPU: 512 Llama-3-8B requests with
+    contexts ~ U[8192, 32768] (≈43 GB of K/V, every segment split and merged
+    in the launch), the step's append fused in; oracle on a sample."""
+    prob = workloads.make_decode_problem(workloads.LLAMA3_8B, 512, 8192, 32768, seed=0,
+                                         device=DEV, num_layers=1)
+    indptr, indices, last = prob.device_tables(DEV)
+    w = fi.BatchDecodeWithPagedKVCacheWrapper(torch.empty(128 << 20, dtype=torch.uint8,
+                                                          device=DEV), "HND")
+    w.plan(indptr, indices, last, 32, 8, 128, 16, q_data_type=torch.bfloat16)
+    out, lse = w.run_with_append(prob.q, prob.pool[0], prob.k_new, prob.v_new,
+                                 _t(prob.positions), return_lse=True)
+    assert torch.isfinite(out).all() and torch.isfinite(lse).all()
+    sample = [0, 1, 255, 511]
+    # the appended rows landed (bit-exact) in the sampled requests' last slots
+    P = 16
+    for b in sample:
+        pos = int(prob.positions[b])
+        page = int(prob.kv_indices[int(prob.kv_indptr[b]) + pos // P])
+        assert torch.equal(prob.pool[0][page, 0, :, pos % P], prob.k_new[b])
+        assert torch.equal(prob.pool[0][page, 1, :, pos % P], prob.v_new[b])
+    want, want_lse = attention.decode(prob.q.cpu(), prob.pool[0], prob.kv_indptr,
+                                      prob.kv_indices, prob.kv_last_page_len, requests=sample)
+    mx, mean, ok = attention.compare(out.cpu()[sample], want[sample], MAX_ABS, MEAN_ABS)
+    assert ok, f"max-abs {mx:.3e} mean-abs {mean:.3e}"
+    assert torch.allclose(lse.cpu()[sample], want_lse[sample], atol=1e-3, rtol=1e-4)
