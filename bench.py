@@ -429,6 +429,11 @@ def run_ours(args):
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     ok = torch.equal(h_out[layers - 1], out.cpu())  # same q, same pool state: same result
     _check(lir, ours, "bench e2e")
+    # configuration 2 is a full decode step: also time the whole model
+    model = (model_step(args, ours, prob, indptr, indices, last, seq, world)
+             if args.workload == "cfg2" and not args.no_model else None)
+    if ours:
+        _check(lir, ours, "bench model step")
 
     peak, peak_kind = _peaks()
     # the timed launch: decode + the step's fused append (ours), decode alone (FlashInfer)
@@ -480,12 +485,119 @@ def run_ours(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if model is not None:
+            line["model_step"] = model
         if not ours:
             _mark_flashinfer(line)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def model_step(args, ours: bool, prob, indptr, indices, last, seq, world: int) -> dict:
+    """Configuration 2's full decode step: a TinyLlama-1.1B-geometry HF LLaMA
+    (22 layers, hidden 2048, MLP 5632, 32 q / 4 kv heads, vocab 32000,
+    RMSNorm, RoPE theta 1e4; random-init bf16 weights) patched with this
+    package's ``llama`` module exactly as the reference engine patches its
+    model, decoding one token for each of the step's requests over the same
+    paged pool. One step = positions + plan + the model forward (22 x
+    qkv GEMM, RoPE + append, paged decode, o_proj, MLP; lm_head).
+
+    FlashInfer's arm runs the same model with the reference's per-layer calls
+    (apply_rope_pos_ids_inplace, append_paged_kv_cache, decode forward; its
+    plan works on the host, so eager only). This package's step is also
+    replayed from a CUDA graph. transformers builds no attention mask for a
+    one-token causal query under its "sdpa" setting; the patched attention
+    reads none either way."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    lm = importlib.import_module(PKG + ".llama")
+    saved = (lm.flashinfer, lm.paged_attention)
+    B = prob.batch
+    dev = prob.pool.device
+    if not ours:
+        import flashinfer as real_fi
+        lm.flashinfer = real_fi
+
+        def fi_paged_attention(attn, q_flat, k_flat, v_flat):
+            st = lm.PagedAttnState
+            layer_kv_cache = st.kv_pool[attn.layer_idx]
+            real_fi.apply_rope_pos_ids_inplace(q_flat, k_flat, st.positions, rotary_dim=None,
+                                               interleave=False, rope_scale=attn.rope_scale,
+                                               rope_theta=attn.rope_theta)
+            real_fi.append_paged_kv_cache(k_flat, v_flat, st.batch_indices, st.positions,
+                                          layer_kv_cache, st.kv_indices, st.kv_indptr,
+                                          st.kv_last_page_len, kv_layout="HND")
+            return st.decode_wrapper.forward(q=q_flat, paged_kv_cache=layer_kv_cache)
+
+        lm.paged_attention = fi_paged_attention
+    try:
+        g = prob.geom
+        cfg = LlamaConfig(vocab_size=32000, hidden_size=2048, intermediate_size=5632,
+                          num_hidden_layers=g.num_layers, num_attention_heads=g.num_qo_heads,
+                          num_key_value_heads=g.num_kv_heads, max_position_embeddings=8192,
+                          rms_norm_eps=1e-5, rope_theta=10000.0)
+        cfg._attn_implementation = "sdpa"
+        torch.manual_seed(0)
+        with torch.device(dev):
+            model = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+        lm.patch_llama_model(model)
+        params = sum(p.numel() for p in model.parameters())
+        lm.init_flashinfer_state(kv_pool=prob.pool, page_size=g.page_size, device=dev)
+        append_indptr = torch.arange(B + 1, dtype=torch.int32, device=dev)
+        ids = torch.randint(0, 32000, (B, 1), device=dev,
+                            generator=torch.Generator(dev).manual_seed(1))
+
+        def step():
+            lm.build_batch_indices_positions(append_indptr, seq, **({"nnz": B} if ours else {}))
+            lm.plan_decode(kv_indptr=indptr, kv_indices=indices, kv_last_page_len=last,
+                           num_qo_heads=g.num_qo_heads, num_kv_heads=g.num_kv_heads,
+                           head_dim=g.head_dim)
+            with torch.no_grad():
+                return model(input_ids=ids, use_cache=False).logits
+
+        stream = torch.cuda.current_stream()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+
+        def timed(run) -> float:
+            _barrier(world)
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for _ in range(args.steps):
+                run()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            return _max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+
+        for _ in range(max(3, args.warmup)):
+            step()
+        eager_ms = timed(step)
+        res = {"model": "TinyLlama-1.1B geometry, random-init bf16 weights",
+               "parameters": params, "requests_per_gpu": B,
+               "eager_ms_per_step": round(eager_ms, 4),
+               "eager_decode_tok_s": round(_sum_over_ranks(B / (eager_ms * 1e-3), world), 1)}
+        if ours and not args.eager:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = step()
+            graph.replay()
+            torch.cuda.synchronize()
+            graph_ms = timed(graph.replay)
+            check = step()
+            torch.cuda.synchronize()
+            res.update({"ms_per_step": round(graph_ms, 4),
+                        "decode_tok_s": round(_sum_over_ranks(B / (graph_ms * 1e-3), world), 1),
+                        "step_launch": "CUDA graph replay",
+                        "graph_logits_equal_eager": bool(torch.equal(logits, check))})
+            del graph
+        else:
+            res.update({"ms_per_step": res["eager_ms_per_step"],
+                        "decode_tok_s": res["eager_decode_tok_s"], "step_launch": "eager"})
+        del model
+        return res
+    finally:
+        lm.flashinfer, lm.paged_attention = saved
 
 
 def _traffic_from_profile(bytes_decode: int):
@@ -765,6 +877,8 @@ def main():
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
                     default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the full-model decode step of configuration 2")
     ap.add_argument("--eager", action="store_true",
                     help="time the decode step with eager launches instead of a CUDA graph")
     args = ap.parse_args()
