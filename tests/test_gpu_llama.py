@@ -119,3 +119,59 @@ def test_patched_model_prefill_then_decode_matches_hf_eager(fi, monkeypatch, fus
                 want = ref(input_ids=t([seqs[i]]), use_cache=False).logits[0, -1]
             rel, cos = _close(logits[i], want)
             assert rel < 0.05 and cos > 0.999, (step, i, rel, cos)
+
+
+def test_patched_model_decode_step_replays_from_cuda_graph(fi):
+    """The patched model's decode step (positions, device plan, forward) is
+    captured once in a CUDA graph and replayed: bit-identical logits to the
+    eager step, also after the step's device inputs change in place.
+    transformers' "sdpa" setting keeps its mask builder off the host for a
+    one-token query (the patched attention reads no mask)."""
+    llama = importlib.import_module("llm-inference-runtime_b200.llama")
+    model = _model()
+    llama.patch_llama_model(model)
+    model.config._attn_implementation = "sdpa"
+    hd = 512 // 8
+    num_pages = 64
+    g = torch.Generator(device=DEV).manual_seed(3)
+    pool = torch.randn((2, num_pages, 2, 2, P, hd), generator=g, device=DEV).to(torch.bfloat16)
+    llama.init_flashinfer_state(kv_pool=pool, page_size=P, device=DEV)
+    lens = [30, 45, 17]
+    rng = np.random.default_rng(4)
+    perm = rng.permutation(num_pages)
+    npages = [math.ceil(L / P) for L in lens]
+    page_ids = [perm[sum(npages[:i]):sum(npages[:i + 1])] for i in range(3)]
+    indptr, indices, last = _tables(lens, npages, page_ids)
+    t = lambda a: torch.as_tensor(a).to(DEV)  # noqa: E731
+    indptr, indices, last = t(indptr), t(indices), t(last)
+    seq = t(np.array(lens, dtype=np.int32))
+    append_indptr = t(np.arange(4, dtype=np.int32))
+    ids = t(rng.integers(0, 512, (3, 1)))
+
+    def step():
+        llama.build_batch_indices_positions(append_indptr, seq, nnz=3)
+        llama.plan_decode(kv_indptr=indptr, kv_indices=indices, kv_last_page_len=last,
+                          num_qo_heads=8, num_kv_heads=2, head_dim=hd)
+        with torch.no_grad():
+            return model(input_ids=ids, use_cache=False).logits[:, -1]
+
+    lir = importlib.import_module("llm-inference-runtime_b200")
+    eager = step().clone()
+    saved = fi._CHECK
+    fi._CHECK = False  # no host synchronisation inside the capture
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = step()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+        ids.copy_(t(rng.integers(0, 512, (3, 1))))  # new tokens, same buffers
+        graph.replay()
+        torch.cuda.synchronize()
+        replayed = out.clone()
+    finally:
+        fi._CHECK = saved
+    assert lir._lib.device_status() == lir._lib.PA_OK
+    assert torch.equal(replayed, step())
+    assert not torch.equal(replayed, eager)
