@@ -434,6 +434,12 @@ def run_ours(args):
              if args.workload == "cfg2" and not args.no_model else None)
     if ours:
         _check(lir, ours, "bench model step")
+    # configuration 4: the same step with the shared prefix attended once
+    cascade = (cascade_step(args, fi, prob, geom, layers, seq, append_indptr, out, small, flush,
+                            world, bytes_step)
+               if args.workload == "cfg4" and ours else None)
+    if ours:
+        _check(lir, ours, "bench cascade step")
 
     peak, peak_kind = _peaks()
     # the timed launch: decode + the step's fused append (ours), decode alone (FlashInfer)
@@ -487,12 +493,87 @@ def run_ours(args):
         }
         if model is not None:
             line["model_step"] = model
+        if cascade is not None:
+            line["cascade"] = cascade
         if not ours:
             _mark_flashinfer(line)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def cascade_step(args, fi, prob, geom, layers, seq, append_indptr, plain_out, small, flush,
+                 world: int, bytes_step: int) -> dict:
+    """Configuration 4 through the two-level cascade wrapper: level 0 the
+    2048-token prefix every request shares (attended once for all requests),
+    level 1 each request's own pages. One step = positions + cascade plan,
+    then per layer the step's KV append and the cascade run; replayed from a
+    CUDA graph, timed like the plain step (L2 flushed before each step).
+    Throughput is reported in the same logical bytes as the plain step."""
+    dev = prob.pool.device
+    B = prob.batch
+    sp = int(prob.extra["shared_pages"])
+    indptr, indices = prob.kv_indptr, prob.kv_indices
+    uniq, uptr = [], [0]
+    for b in range(B):
+        pages = indices[indptr[b]:indptr[b + 1]]
+        uniq.append(pages[sp:])
+        uptr.append(uptr[-1] + len(pages) - sp)
+    t = lambda a: torch.as_tensor(np.asarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+    s_indptr, s_indices, s_last = t([0, sp]), t(indices[:sp]), t([geom.page_size])
+    u_indptr, u_indices = t(uptr), t(np.concatenate(uniq))
+    u_last = t(prob.kv_last_page_len)
+    full_indptr, full_indices, full_last = prob.device_tables(dev)
+    ws = torch.empty(max(fi.cascade_workspace_bytes(B, geom.num_qo_heads, geom.num_kv_heads,
+                                                    geom.head_dim), 1 << 20),
+                     dtype=torch.uint8, device=dev)
+    w = fi.MultiLevelCascadeAttentionWrapper(2, ws, "HND")
+    out = torch.empty_like(prob.q)
+    qo_levels = [torch.tensor([0, B], dtype=torch.int32),
+                 torch.arange(B + 1, dtype=torch.int32)]
+
+    def step():
+        bi, pos = fi.get_batch_indices_positions(append_indptr, seq, B)
+        w.plan(qo_levels, [s_indptr, u_indptr], [s_indices, u_indices], [s_last, u_last],
+               geom.num_qo_heads, geom.num_kv_heads, geom.head_dim, geom.page_size)
+        for layer in range(layers):
+            fi.append_paged_kv_cache(prob.k_new, prob.v_new, bi, pos, prob.pool[layer],
+                                     full_indices, full_indptr, full_last, kv_layout="HND")
+            w.run(prob.q, prob.pool[layer], out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    total = 0.0
+    for _ in range(args.steps):
+        if small:
+            flush.view(torch.int64).sum()
+        t0.record(stream)
+        graph.replay()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        total += t0.elapsed_time(t1)
+    ms = _max_over_ranks(total / args.steps, world)
+    diff = (out.float() - plain_out.float()).abs()
+    mx, mean = float(diff.max()), float(diff.mean())
+    del graph
+    return {"levels": f"level 0: {sp} shared pages, level 1: each request's own pages",
+            "ms_per_step": round(ms, 4),
+            "value": round(_sum_over_ranks(float(bytes_step), world) / (ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s (logical bytes, as the plain step)",
+            "step_launch": "CUDA graph replay",
+            "matches_plain_step": {"max_abs": round(mx, 5), "mean_abs": round(mean, 6),
+                                   "within_tolerance": bool(mx <= 2e-2 and mean <= 2e-3)}}
 
 
 def model_step(args, ours: bool, prob, indptr, indices, last, seq, world: int) -> dict:

@@ -260,6 +260,34 @@ int pa_decode_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
                          void* workspace, size_t workspace_bytes, void* out, float* lse,
                          void* stream);
 
+/* Two-level (cascade) decode, FlashInfer's MultiLevelCascadeAttentionWrapper
+ * with two levels, for a batch whose requests all begin with the same shared
+ * prefix pages — what the reference's RadixCache produces when requests share
+ * a system prompt (src/engine/memory/radix_cache.py:28-88). The reference
+ * decodes such a batch with BatchDecodeWithPagedKVCacheWrapper over each
+ * request's full table (src/models/llama.py:230-245), reading the prefix
+ * once per request; here it is attended once for all requests.
+ *   level 0: shared_kv_indptr = {0, n0}, shared_kv_indices[n0],
+ *            shared_kv_last_page_len[1] — the prefix pages;
+ *   level 1: unique_kv_indptr[B+1], unique_kv_indices,
+ *            unique_kv_last_page_len[B] — each request's pages after it
+ *            (a request may have none).
+ * Output equals decoding each request over prefix + unique pages, within the
+ * bf16 tolerance. Plan once per step (device side, no host synchronisation);
+ * run per layer. */
+size_t pa_cascade_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
+                                  int32_t head_dim);
+int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_last_page_len,
+                    const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
+                    int32_t batch_size, int64_t num_unique_indices, int32_t num_qo_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, void* workspace,
+                    size_t workspace_bytes, void* stream);
+int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                   const int32_t* shared_kv_indices, const int32_t* unique_kv_indices,
+                   const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
+                   int32_t batch_size, int32_t num_qo_heads, float sm_scale, void* workspace,
+                   size_t workspace_bytes, void* out, float* lse, void* stream);
+
 /* Workspace bytes pa_prefill_plan needs. */
 size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int32_t num_qo_heads,
                                   int32_t num_kv_heads, int32_t head_dim);

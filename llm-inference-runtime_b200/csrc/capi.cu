@@ -16,6 +16,7 @@
 #include "prefill.cuh"
 #include "tables.cuh"
 #include "qkv.cuh"
+#include "cascade.cuh"
 
 namespace {
 
@@ -931,6 +932,7 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.hdr = reinterpret_cast<const PrefillPlanHeader*>(ws + L.hdr);
   p.items = reinterpret_cast<const int4*>(ws + L.items);
+  p.q_rows = nullptr;
   const int dev = current_device();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cache->dtype == PA_DTYPE_BF16)
@@ -938,6 +940,165 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
                    : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, p, max_items, dev, s);
   return D == 64 ? launch_prefill<__half, 64>(qm, km, vm, p, max_items, dev, s)
                  : launch_prefill<__half, 128>(qm, km, vm, p, max_items, dev, s);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Cascade geometry for a batch: level-0 chunk count sized so the chunks'
+// prefill items fill the SMs once, the decode partition of level 1, and the
+// workspace layout of both.
+struct CascadeShape {
+  int qt, span, max_chunks;
+  DecodePlanShape dec;
+  CascadeWsLayout L;
+};
+
+bool cascade_shape(int dev, int batch, int hq, int hkv, int head_dim, CascadeShape* s) {
+  if (batch <= 0 || hq <= 0 || hkv <= 0 || hq % hkv) return false;
+  if (!decode_shape(dev, hkv, head_dim, &s->dec)) return false;
+  s->qt = prefill_qt(hq / hkv);
+  if (s->qt == 0) return false;
+  s->span = 2 * s->qt;
+  const int nq = (batch + s->span - 1) / s->span;
+  const int per_chunk = hkv * nq;
+  s->max_chunks = std::max(1, std::min((s->dec.ctas + per_chunk - 1) / per_chunk,
+                                       kCascadeMaxChunks));
+  s->L = cascade_ws_layout(batch, hq, hkv, head_dim, s->max_chunks, s->span, s->dec.units,
+                           s->dec.g.hb);
+  return true;
+}
+
+template <typename T, int D>
+int launch_cascade_merge(const CascadeWsLayout& L, uint8_t* ws, int batch, int hq, void* out,
+                         float* lse, cudaStream_t s) {
+  const int64_t threads = static_cast<int64_t>(batch) * hq * 32;
+  const int blocks = static_cast<int>((threads + 255) / 256);
+  return launch_chain(cascade_merge_kernel<T, D>, dim3(blocks), dim3(256), 0, s,
+                      reinterpret_cast<const T*>(ws + L.o0),
+                      reinterpret_cast<const float*>(ws + L.lse0),
+                      reinterpret_cast<const T*>(ws + L.o1),
+                      reinterpret_cast<const float*>(ws + L.lse1),
+                      reinterpret_cast<const CascadeHeader*>(ws + L.hdr), batch, hq,
+                      static_cast<T*>(out), lse);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t pa_cascade_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
+                                  int32_t head_dim) {
+  CascadeShape sh;
+  if (!cascade_shape(current_device(), batch_size, num_qo_heads, num_kv_heads, head_dim, &sh))
+    return 0;
+  return sh.L.total;
+}
+
+int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_last_page_len,
+                    const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
+                    int32_t batch_size, int64_t num_unique_indices, int32_t num_qo_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (shared_kv_indptr == nullptr || shared_kv_last_page_len == nullptr ||
+      unique_kv_indptr == nullptr || unique_kv_last_page_len == nullptr || workspace == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (batch_size <= 0 || num_unique_indices < 0 || num_qo_heads <= 0 || num_kv_heads <= 0 ||
+      num_qo_heads % num_kv_heads)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (head_dim != 64 && head_dim != 128) return PA_ERR_UNSUPPORTED;
+  if (page_size != kPage) return PA_ERR_UNSUPPORTED;
+  if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
+  CascadeShape sh;
+  if (!cascade_shape(current_device(), batch_size, num_qo_heads, num_kv_heads, head_dim, &sh))
+    return PA_ERR_UNSUPPORTED;
+  if (sh.L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = launch_chain(cascade_plan_kernel, dim3(1), dim3(256), 0, s, shared_kv_indptr,
+                        shared_kv_last_page_len, batch_size, num_qo_heads, num_kv_heads,
+                        head_dim, page_size, sh.qt, sh.max_chunks, ws, sh.L);
+  if (st != PA_OK) return st;
+  return pa_decode_plan(unique_kv_indptr, unique_kv_last_page_len, batch_size,
+                        num_unique_indices, num_qo_heads, num_kv_heads, head_dim, page_size,
+                        ws + sh.L.decode, sh.L.o0 - sh.L.decode, stream);
+}
+
+int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                   const int32_t* shared_kv_indices, const int32_t* unique_kv_indices,
+                   const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
+                   int32_t batch_size, int32_t num_qo_heads, float sm_scale, void* workspace,
+                   size_t workspace_bytes, void* out, float* lse, void* stream) {
+  int st = check_cache(cache);
+  if (st != PA_OK) return st;
+  if (q == nullptr || out == nullptr || shared_kv_indices == nullptr ||
+      unique_kv_indices == nullptr || unique_kv_indptr == nullptr ||
+      unique_kv_last_page_len == nullptr || workspace == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  const int hkv = cache->num_kv_heads, D = cache->head_dim;
+  if (batch_size <= 0 || num_qo_heads <= 0 || num_qo_heads % hkv) return PA_ERR_INVALID_ARGUMENT;
+  if (D != 64 && D != 128) return PA_ERR_UNSUPPORTED;
+  if (cache->page_size != kPage) return PA_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(out) || q_stride_n % 8 || q_stride_h % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  const int dev = current_device();
+  CascadeShape sh;
+  if (!cascade_shape(dev, batch_size, num_qo_heads, hkv, D, &sh)) return PA_ERR_UNSUPPORTED;
+  const CascadeWsLayout& L = sh.L;
+  if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int G = num_qo_heads / hkv;
+  // ---- level 0: the shared prefix, key chunks as non-causal prefill requests
+  CUtensorMap qm, km, vm;
+  if ((st = encode_q_map(&qm, q, q_stride_n, q_stride_h, batch_size, num_qo_heads, D, G, sh.qt,
+                         cache->dtype)) != PA_OK)
+    return st;
+  if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage, 1)) != PA_OK) return st;
+  if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage, 1)) != PA_OK) return st;
+  const PrefillWsLayout PL = prefill_ws_layout(L.prefill_items);
+  PrefillParams p;
+  p.out = ws + L.o0;
+  p.lse = reinterpret_cast<float*>(ws + L.lse0);
+  p.qo_indptr = reinterpret_cast<const int32_t*>(ws + L.qo_indptr);
+  p.kv_indptr = reinterpret_cast<const int32_t*>(ws + L.kv_indptr);
+  p.kv_indices = shared_kv_indices;
+  p.kv_last_page_len = reinterpret_cast<const int32_t*>(ws + L.last);
+  p.batch_size = sh.max_chunks;
+  p.num_qo_heads = num_qo_heads;
+  p.num_kv_heads = hkv;
+  p.group = G;
+  p.qt = sh.qt;
+  p.causal = 0;
+  p.num_pages = cache->num_pages;
+  p.heads_inner = heads_inner(*cache) ? 1 : 0;
+  const float scale = sm_scale > 0.f ? sm_scale : 1.0f / std::sqrt(static_cast<float>(D));
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.hdr = reinterpret_cast<const PrefillPlanHeader*>(ws + L.prefill + PL.hdr);
+  p.items = reinterpret_cast<const int4*>(ws + L.prefill + PL.items);
+  p.q_rows = reinterpret_cast<const int32_t*>(ws + L.q_rows);
+  const bool bf16 = cache->dtype == PA_DTYPE_BF16;
+  st = bf16 ? (D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, p, L.prefill_items, dev, s)
+                       : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, p, L.prefill_items, dev, s))
+            : (D == 64 ? launch_prefill<__half, 64>(qm, km, vm, p, L.prefill_items, dev, s)
+                       : launch_prefill<__half, 128>(qm, km, vm, p, L.prefill_items, dev, s));
+  if (st != PA_OK) return st;
+  // ---- level 1: each request's unique pages
+  st = decode_run(q, q_stride_n, q_stride_h, cache, unique_kv_indices, unique_kv_indptr,
+                  unique_kv_last_page_len, batch_size, num_qo_heads, sm_scale, ws + L.decode,
+                  L.o0 - L.decode, ws + L.o1, reinterpret_cast<float*>(ws + L.lse1), stream,
+                  nullptr);
+  if (st != PA_OK) return st;
+  // ---- merge
+  return bf16 ? (D == 64 ? launch_cascade_merge<__nv_bfloat16, 64>(L, ws, batch_size,
+                                                                   num_qo_heads, out, lse, s)
+                         : launch_cascade_merge<__nv_bfloat16, 128>(L, ws, batch_size,
+                                                                    num_qo_heads, out, lse, s))
+              : (D == 64 ? launch_cascade_merge<__half, 64>(L, ws, batch_size, num_qo_heads, out,
+                                                            lse, s)
+                         : launch_cascade_merge<__half, 128>(L, ws, batch_size, num_qo_heads,
+                                                             out, lse, s));
 }
 
 }  // extern "C"

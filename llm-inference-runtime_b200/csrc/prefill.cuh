@@ -168,6 +168,10 @@ struct PrefillParams {
   float scale_log2;
   const PrefillPlanHeader* hdr;
   const int4* items;
+  // Optional: first q row of request b (default qo_indptr[b]). Lets several
+  // requests read the same queries while writing their own output rows —
+  // the key chunks of a shared prefix (cascade decode).
+  const int32_t* q_rows;
 };
 
 // --------------------------------------------------------------------- plan
@@ -303,6 +307,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   const int G = p.group, QT = p.qt, hq = p.num_qo_heads;
   const int qo_start = __ldg(p.qo_indptr + b);
   const int qo_len = __ldg(p.qo_indptr + b + 1) - qo_start;
+  const int q_row0 = p.q_rows != nullptr ? __ldg(p.q_rows + b) : qo_start;
   const int page0 = __ldg(p.kv_indptr + b);
   const int npages = __ldg(p.kv_indptr + b + 1) - page0;
   const int kv_len = npages > 0 ? (npages - 1) * kPage + __ldg(p.kv_last_page_len + b) : 0;
@@ -349,7 +354,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
           tma_load_3d(sQ + t * C::kQBytes + pn * C::kPanelBytes, &qmap, q_full, pn * 64, h * G,
-                      qo_start + t0 + t * QT);
+                      q_row0 + t0 + t * QT);
     }
     for (int j = 0; j < ntiles && !failed; ++j) {
       const int st = j % S, use = j / S;

@@ -542,3 +542,109 @@ class BatchPrefillWithPagedKVCacheWrapper:
         if sm_scale is not None:
             self._sm_scale = sm_scale
         return self.run(q, paged_kv_cache, k_scale=k_scale, v_scale=v_scale, return_lse=True)
+
+
+class MultiLevelCascadeAttentionWrapper:
+    """This package's two-level cascade decode (FlashInfer's wrapper of this
+    name, the subset a radix-shared batch needs): level 0 holds the prefix
+    pages every request shares (one group: ``qo_indptr_arr[0] = [0, B]``),
+    level 1 each request's pages after it (``qo_indptr_arr[1] = arange(B+1)``,
+    one decode query per request). The prefix is attended once for all
+    requests instead of once per request, as the reference's per-request
+    decode (src/models/llama.py:230-245) does. Tables live on the device; the
+    plan never synchronises with the host."""
+
+    def __init__(self, num_levels: int, float_workspace_buffer: torch.Tensor,
+                 kv_layout: str = "NHD", use_cuda_graph: bool = False, **kwargs) -> None:
+        if num_levels != 2:
+            raise NotImplementedError("only two levels (shared prefix + unique pages)")
+        if kv_layout not in ("NHD", "HND"):
+            raise KeyError(f"Invalid kv_layout {kv_layout}")
+        self._ws = float_workspace_buffer
+        self._kv_layout = kv_layout
+        self._planned = False
+
+    def reset_workspace_buffer(self, float_workspace_buffer: torch.Tensor, *args) -> None:
+        self._ws = float_workspace_buffer
+
+    def plan(self, qo_indptr_arr, paged_kv_indptr_arr, paged_kv_indices_arr,
+             paged_kv_last_page_len_arr, num_qo_heads: int, num_kv_heads: int, head_dim: int,
+             page_size: int, causal: bool = False, pos_encoding_mode: str = "NONE",
+             window_left: int = -1, logits_soft_cap: Optional[float] = None,
+             sm_scale: Optional[float] = None, q_data_type="float16", kv_data_type=None,
+             **kwargs) -> None:
+        _check_plan_options(pos_encoding_mode, window_left, logits_soft_cap)
+        if len(qo_indptr_arr) != 2:
+            raise NotImplementedError("only two levels (shared prefix + unique pages)")
+        qo0, qo1 = qo_indptr_arr
+        batch = qo1.numel() - 1
+        if qo0.numel() != 2 or batch <= 0 or paged_kv_indptr_arr[0].numel() != 2:
+            raise NotImplementedError("level 0 must be one prefix shared by every request")
+        for name, t in (("qo_indptr_arr[0]", qo0), ("qo_indptr_arr[1]", qo1)):
+            if t.device.type == "cpu":  # values are checked only where that costs no sync
+                want = [0, batch] if name.endswith("[0]") else list(range(batch + 1))
+                if t.tolist() != want:
+                    raise NotImplementedError(f"{name} must be {want[:4]}...: one decode "
+                                              "query per request, all sharing level 0")
+        device = self._ws.device
+        self._shared_indptr = _i32_on(paged_kv_indptr_arr[0], device, "paged_kv_indptr_arr[0]")
+        self._shared_indices = _i32_on(paged_kv_indices_arr[0], device,
+                                       "paged_kv_indices_arr[0]")
+        self._shared_last = _i32_on(paged_kv_last_page_len_arr[0], device,
+                                    "paged_kv_last_page_len_arr[0]")
+        self._indptr = _i32_on(paged_kv_indptr_arr[1], device, "paged_kv_indptr_arr[1]")
+        self._indices = _i32_on(paged_kv_indices_arr[1], device, "paged_kv_indices_arr[1]")
+        self._last = _i32_on(paged_kv_last_page_len_arr[1], device,
+                             "paged_kv_last_page_len_arr[1]")
+        # an empty level (no shared prefix, or no request with pages of its
+        # own) still passes a valid pointer; the kernels read no entry of it
+        if self._shared_indices.numel() == 0:
+            self._shared_indices = torch.zeros(1, dtype=torch.int32, device=device)
+        if self._indices.numel() == 0:
+            self._indices = torch.zeros(1, dtype=torch.int32, device=device)
+        self._batch, self._hq, self._hkv, self._d, self._p = (batch, num_qo_heads, num_kv_heads,
+                                                             head_dim, page_size)
+        self._sm_scale = sm_scale
+        _lib.check(_lib.load().pa_cascade_plan(
+            _p(self._shared_indptr), _p(self._shared_last), _p(self._indptr), _p(self._last),
+            batch, self._indices.numel(), num_qo_heads, num_kv_heads, head_dim, page_size,
+            _p(self._ws), self._ws.numel() * self._ws.element_size(), _stream()),
+            "MultiLevelCascadeAttentionWrapper.plan")
+        _after("MultiLevelCascadeAttentionWrapper.plan")
+        self._planned = True
+
+    def run(self, q: torch.Tensor, paged_kv_cache, out: Optional[torch.Tensor] = None,
+            lse: Optional[torch.Tensor] = None, return_lse: bool = False):
+        if not self._planned:
+            raise RuntimeError("plan() must be called before run()")
+        desc = kv_cache_desc(paged_kv_cache, self._kv_layout)
+        if (desc.num_kv_heads, desc.head_dim, desc.page_size) != (self._hkv, self._d, self._p):
+            raise ValueError("paged_kv_cache geometry differs from the plan")
+        if _dtype_code(q.dtype) != desc.dtype:
+            raise NotImplementedError("q and the KV cache must have the same dtype")
+        qsn, qsh = _row_strides(q, "q")
+        if tuple(q.shape) != (self._batch, self._hq, self._d):
+            raise ValueError(f"q must be [{self._batch}, {self._hq}, {self._d}]")
+        if out is None:
+            out = torch.empty_like(q, memory_format=torch.contiguous_format)
+        elif not out.is_contiguous() or tuple(out.shape) != tuple(q.shape):
+            raise ValueError("out must be a contiguous [batch, num_qo_heads, head_dim] tensor")
+        if return_lse and lse is None:
+            lse = torch.empty((self._batch, self._hq), dtype=torch.float32, device=q.device)
+        scale = self._sm_scale if self._sm_scale is not None else 1.0 / math.sqrt(self._d)
+        _lib.check(_lib.load().pa_cascade_run(
+            _p(q), qsn, qsh, ctypes.byref(desc), _p(self._shared_indices), _p(self._indices),
+            _p(self._indptr), _p(self._last), self._batch, self._hq, float(scale), _p(self._ws),
+            self._ws.numel() * self._ws.element_size(), _p(out), _p(lse), _stream()),
+            "MultiLevelCascadeAttentionWrapper.run")
+        _after("MultiLevelCascadeAttentionWrapper.run")
+        return (out, lse) if return_lse else out
+
+    forward = run
+
+
+def cascade_workspace_bytes(batch_size: int, num_qo_heads: int, num_kv_heads: int,
+                            head_dim: int) -> int:
+    """Workspace bytes MultiLevelCascadeAttentionWrapper needs (this package)."""
+    return int(_lib.load().pa_cascade_workspace_bytes(batch_size, num_qo_heads, num_kv_heads,
+                                                      head_dim))
