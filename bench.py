@@ -508,8 +508,9 @@ def cascade_step(args, fi, prob, geom, layers, seq, append_indptr, plain_out, sm
     """Configuration 4 through the two-level cascade wrapper: level 0 the
     2048-token prefix every request shares (attended once for all requests),
     level 1 each request's own pages. One step = positions + cascade plan,
-    then per layer the step's KV append and the cascade run; replayed from a
+    then per layer the cascade run with the step's KV append; replayed from a
     CUDA graph, timed like the plain step (L2 flushed before each step).
+    The append is fused into the level-1 decode, as the plain step fuses it.
     Throughput is reported in the same logical bytes as the plain step."""
     dev = prob.pool.device
     B = prob.batch
@@ -524,7 +525,6 @@ def cascade_step(args, fi, prob, geom, layers, seq, append_indptr, plain_out, sm
     s_indptr, s_indices, s_last = t([0, sp]), t(indices[:sp]), t([geom.page_size])
     u_indptr, u_indices = t(uptr), t(np.concatenate(uniq))
     u_last = t(prob.kv_last_page_len)
-    full_indptr, full_indices, full_last = prob.device_tables(dev)
     ws = torch.empty(max(fi.cascade_workspace_bytes(B, geom.num_qo_heads, geom.num_kv_heads,
                                                     geom.head_dim), 1 << 20),
                      dtype=torch.uint8, device=dev)
@@ -534,13 +534,11 @@ def cascade_step(args, fi, prob, geom, layers, seq, append_indptr, plain_out, sm
                  torch.arange(B + 1, dtype=torch.int32)]
 
     def step():
-        bi, pos = fi.get_batch_indices_positions(append_indptr, seq, B)
+        _, pos = fi.get_batch_indices_positions(append_indptr, seq, B)
         w.plan(qo_levels, [s_indptr, u_indptr], [s_indices, u_indices], [s_last, u_last],
                geom.num_qo_heads, geom.num_kv_heads, geom.head_dim, geom.page_size)
         for layer in range(layers):
-            fi.append_paged_kv_cache(prob.k_new, prob.v_new, bi, pos, prob.pool[layer],
-                                     full_indices, full_indptr, full_last, kv_layout="HND")
-            w.run(prob.q, prob.pool[layer], out=out)
+            w.run_with_append(prob.q, prob.pool[layer], prob.k_new, prob.v_new, pos, out=out)
 
     for _ in range(max(3, args.warmup)):
         step()

@@ -288,6 +288,23 @@ int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
                    int32_t batch_size, int32_t num_qo_heads, float sm_scale, void* workspace,
                    size_t workspace_bytes, void* out, float* lse, void* stream);
 
+/* pa_cascade_run with the decode step's KV append fused into level 1, as
+ * pa_decode_append_run does for the plain decode: row b of append_key /
+ * append_value goes to global position positions[b] of request b (the
+ * reference's append_paged_kv_cache, src/models/llama.py:188-210), which must
+ * fall inside the request's level-1 pages (position - prefix keys in
+ * [0, keys of level 1)); otherwise the device status reports
+ * PA_ERR_DEVICE_CHECK. Shared prefix pages are never written. */
+int pa_cascade_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                          const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
+                          const void* append_value, int64_t value_stride_n,
+                          int64_t value_stride_h, const int32_t* positions,
+                          const pa_kv_cache* cache, const int32_t* shared_kv_indices,
+                          const int32_t* unique_kv_indices, const int32_t* unique_kv_indptr,
+                          const int32_t* unique_kv_last_page_len, int32_t batch_size,
+                          int32_t num_qo_heads, float sm_scale, void* workspace,
+                          size_t workspace_bytes, void* out, float* lse, void* stream);
+
 /* Workspace bytes pa_prefill_plan needs. */
 size_t pa_prefill_workspace_bytes(int32_t batch_size, int64_t max_total_qo, int32_t num_qo_heads,
                                   int32_t num_kv_heads, int32_t head_dim);

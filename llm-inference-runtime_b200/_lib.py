@@ -125,6 +125,12 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int64, POINTER(PagedKVCache), c_void_p, c_void_p, c_void_p,
          c_void_p, c_int32, c_int32, c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p],
     ),
+    "pa_cascade_append_run": (
+        c_int32,
+        [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64,
+         c_void_p, POINTER(PagedKVCache), c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+         c_float, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p],
+    ),
     "pa_prefill_workspace_bytes": (c_size_t, [c_int32, c_int64, c_int32, c_int32, c_int32]),
     "pa_prefill_plan": (
         c_int32,

@@ -5,6 +5,7 @@
 #include <atomic>
 #include <type_traits>
 #include <cmath>
+#include <cstddef>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -703,6 +704,7 @@ struct DecodeAppend {
   const void* value;
   int64_t value_stride_n, value_stride_h;
   const int32_t* positions;
+  const int32_t* pos_base;  // device word subtracted from each position, or nullptr
 };
 
 int decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
@@ -762,6 +764,7 @@ int decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_k
   p.part_lse = reinterpret_cast<float*>(ws + L.part_lse);
   p.part_o = reinterpret_cast<float*>(ws + L.part_o);
   p.append_pos = nullptr;
+  p.append_pos_base = nullptr;
   p.new_k = p.new_v = nullptr;
   p.new_k_stride_n = p.new_k_stride_h = p.new_v_stride_n = p.new_v_stride_h = 0;
   p.k_pool = p.v_pool = nullptr;
@@ -769,6 +772,7 @@ int decode_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_k
   if (app != nullptr) {
     const int esz = 2;  // bf16 / fp16
     p.append_pos = app->positions;
+    p.append_pos_base = app->pos_base;
     p.new_k = static_cast<const uint8_t*>(app->key);
     p.new_v = static_cast<const uint8_t*>(app->value);
     p.new_k_stride_n = app->key_stride_n * esz;
@@ -820,7 +824,7 @@ int pa_decode_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
       key_stride_h % 8 || value_stride_n % 8 || value_stride_h % 8)
     return PA_ERR_INVALID_ARGUMENT;
   const DecodeAppend app{append_key, key_stride_n, key_stride_h, append_value,
-                         value_stride_n, value_stride_h, positions};
+                         value_stride_n, value_stride_h, positions, nullptr};
   return decode_run(q, q_stride_n, q_stride_h, cache, kv_indices, kv_indptr, kv_last_page_len,
                     batch_size, num_qo_heads, sm_scale, workspace, workspace_bytes, out, lse,
                     stream, &app);
@@ -1025,11 +1029,18 @@ int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_la
                         ws + sh.L.decode, sh.L.o0 - sh.L.decode, stream);
 }
 
-int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
-                   const int32_t* shared_kv_indices, const int32_t* unique_kv_indices,
-                   const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
-                   int32_t batch_size, int32_t num_qo_heads, float sm_scale, void* workspace,
-                   size_t workspace_bytes, void* out, float* lse, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Level 0 (prefill over the prefix chunks), level 1 (decode over the unique
+// pages, with the step's append fused in when `app` is given), merge.
+int cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                const int32_t* shared_kv_indices, const int32_t* unique_kv_indices,
+                const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
+                int32_t batch_size, int32_t num_qo_heads, float sm_scale, void* workspace,
+                size_t workspace_bytes, void* out, float* lse, void* stream,
+                const DecodeAppend* app) {
   int st = check_cache(cache);
   if (st != PA_OK) return st;
   if (q == nullptr || out == nullptr || shared_kv_indices == nullptr ||
@@ -1084,11 +1095,18 @@ int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
             : (D == 64 ? launch_prefill<__half, 64>(qm, km, vm, p, L.prefill_items, dev, s)
                        : launch_prefill<__half, 128>(qm, km, vm, p, L.prefill_items, dev, s));
   if (st != PA_OK) return st;
-  // ---- level 1: each request's unique pages
+  // ---- level 1: each request's unique pages (positions of an appended token
+  // are global; the plan recorded the prefix length they are taken from)
+  DecodeAppend app1;
+  if (app != nullptr) {
+    app1 = *app;
+    app1.pos_base = reinterpret_cast<const int32_t*>(ws + L.hdr +
+                                                     offsetof(CascadeHeader, prefix_tokens));
+  }
   st = decode_run(q, q_stride_n, q_stride_h, cache, unique_kv_indices, unique_kv_indptr,
                   unique_kv_last_page_len, batch_size, num_qo_heads, sm_scale, ws + L.decode,
                   L.o0 - L.decode, ws + L.o1, reinterpret_cast<float*>(ws + L.lse1), stream,
-                  nullptr);
+                  app != nullptr ? &app1 : nullptr);
   if (st != PA_OK) return st;
   // ---- merge
   return bf16 ? (D == 64 ? launch_cascade_merge<__nv_bfloat16, 64>(L, ws, batch_size,
@@ -1099,6 +1117,41 @@ int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
                                                             lse, s)
                          : launch_cascade_merge<__half, 128>(L, ws, batch_size, num_qo_heads,
                                                              out, lse, s));
+}
+
+}  // namespace
+
+extern "C" {
+
+int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
+                   const int32_t* shared_kv_indices, const int32_t* unique_kv_indices,
+                   const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
+                   int32_t batch_size, int32_t num_qo_heads, float sm_scale, void* workspace,
+                   size_t workspace_bytes, void* out, float* lse, void* stream) {
+  return cascade_run(q, q_stride_n, q_stride_h, cache, shared_kv_indices, unique_kv_indices,
+                     unique_kv_indptr, unique_kv_last_page_len, batch_size, num_qo_heads,
+                     sm_scale, workspace, workspace_bytes, out, lse, stream, nullptr);
+}
+
+int pa_cascade_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
+                          const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
+                          const void* append_value, int64_t value_stride_n,
+                          int64_t value_stride_h, const int32_t* positions,
+                          const pa_kv_cache* cache, const int32_t* shared_kv_indices,
+                          const int32_t* unique_kv_indices, const int32_t* unique_kv_indptr,
+                          const int32_t* unique_kv_last_page_len, int32_t batch_size,
+                          int32_t num_qo_heads, float sm_scale, void* workspace,
+                          size_t workspace_bytes, void* out, float* lse, void* stream) {
+  if (append_key == nullptr || append_value == nullptr || positions == nullptr)
+    return PA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(append_key) || !aligned16(append_value) || key_stride_n % 8 ||
+      key_stride_h % 8 || value_stride_n % 8 || value_stride_h % 8)
+    return PA_ERR_INVALID_ARGUMENT;
+  const DecodeAppend app{append_key, key_stride_n, key_stride_h, append_value,
+                         value_stride_n, value_stride_h, positions, nullptr};
+  return cascade_run(q, q_stride_n, q_stride_h, cache, shared_kv_indices, unique_kv_indices,
+                     unique_kv_indptr, unique_kv_last_page_len, batch_size, num_qo_heads,
+                     sm_scale, workspace, workspace_bytes, out, lse, stream, &app);
 }
 
 }  // extern "C"

@@ -32,7 +32,8 @@ struct CascadeHeader {
   int32_t pages_per_chunk;
   int32_t batch_size;
   int32_t max_chunks;
-  int32_t reserved[10];
+  int32_t prefix_tokens;    // keys of level 0; level-1 positions start here
+  int32_t reserved[9];
 };
 
 // Byte offsets inside the caller's workspace (all 256-byte aligned).
@@ -135,6 +136,7 @@ __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
     ch->pages_per_chunk = ppc;
     ch->batch_size = batch;
     ch->max_chunks = max_chunks;
+    ch->prefix_tokens = nch > 0 ? (n0 - 1) * page_size + lp : 0;
     ch->magic = kCascadeMagic;
     if (bad) set_status(PA_ERR_DEVICE_CHECK);
   }
@@ -142,47 +144,78 @@ __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
 
 // One warp per (request, q head): log-sum-exp merge of the non-empty level-0
 // chunk states (rows c * B + b) and the level-1 state (row b). Base-2 LSEs;
-// a state with LSE -inf (no keys) contributes nothing.
+// a state with LSE -inf (no keys) contributes nothing. The chunk LSEs are
+// read at once (chunk c in lane c & 31, slot c >> 5), and the state rows in
+// batches of kRows independent loads, so the warp waits on memory a few times
+// rather than once per chunk.
 template <typename T, int D>
 __global__ void cascade_merge_kernel(const T* __restrict__ o0, const float* __restrict__ lse0,
                                      const T* __restrict__ o1, const float* __restrict__ lse1,
                                      const CascadeHeader* __restrict__ ch, int batch, int hq,
                                      T* __restrict__ out, float* __restrict__ lse) {
+  static_assert(kCascadeMaxChunks <= 64, "two LSE slots per lane");
   griddep_wait();
   griddep_launch_dependents();
   constexpr int PER = D / 32;  // elements per lane
+  constexpr int kRows = 8;
+  struct alignas(2 * PER) Row { T e[PER]; };
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= batch * hq) return;
   if (ch->magic != kCascadeMagic || ch->batch_size != batch) {
     if (warp == 0 && lane == 0) set_status(PA_ERR_NOT_PLANNED);
     return;
   }
-  const int b = warp / hq, h = warp - b * hq;
-  const int nch = ch->status == PA_OK ? ch->num_chunks : 0;
-  float m = -INFINITY, w = 0.f, acc[PER];
+  const int nch = ch->status == PA_OK ? min(ch->num_chunks, kCascadeMaxChunks) : 0;
+  const size_t r1 = static_cast<size_t>(warp);          // row b * hq + h
+  const size_t step = static_cast<size_t>(batch) * hq;  // rows from chunk c to c + 1
+  const float la = lane < nch ? __ldg(lse0 + lane * step + r1) : -INFINITY;
+  const float lb = lane + 32 < nch ? __ldg(lse0 + (lane + 32) * step + r1) : -INFINITY;
+  const float l1 = __ldg(lse1 + r1);
+  float m = fmaxf(la, lb);
 #pragma unroll
-  for (int e = 0; e < PER; ++e) acc[e] = 0.f;
-  auto take = [&](const T* row, float l) {
-    if (l == -INFINITY) return;
-    const float mn = fmaxf(m, l);
-    const float sc = ex2(m - mn), wt = ex2(l - mn);
-#pragma unroll
-    for (int e = 0; e < PER; ++e) acc[e] = acc[e] * sc + wt * static_cast<float>(row[lane * PER + e]);
-    w = w * sc + wt;
-    m = mn;
-  };
-  for (int c = 0; c < nch; ++c) {
-    const size_t r = (static_cast<size_t>(c) * batch + b) * hq + h;
-    take(o0 + r * D, __ldg(lse0 + r));
-  }
-  const size_t r1 = static_cast<size_t>(b) * hq + h;
-  take(o1 + r1 * D, __ldg(lse1 + r1));
-  const float inv = w > 0.f ? 1.f / w : 0.f;
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  m = fmaxf(m, l1);
   T* orow = out + r1 * D + lane * PER;
+  if (m == -INFINITY) {  // no keys at either level
+#pragma unroll
+    for (int e = 0; e < PER; e += 2) *reinterpret_cast<uint32_t*>(orow + e) = 0u;
+    if (lse != nullptr && lane == 0) lse[r1] = -INFINITY;
+    return;
+  }
+  const float wa = la == -INFINITY ? 0.f : ex2(la - m);
+  const float wb = lb == -INFINITY ? 0.f : ex2(lb - m);
+  const float w1 = l1 == -INFINITY ? 0.f : ex2(l1 - m);
+  float w = wa + wb;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+  w += w1;
+  float acc[PER];
+  {
+    const Row v = *reinterpret_cast<const Row*>(o1 + r1 * D + lane * PER);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) acc[e] = w1 > 0.f ? w1 * static_cast<float>(v.e[e]) : 0.f;
+  }
+  for (int c0 = 0; c0 < nch; c0 += kRows) {
+    Row v[kRows];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (c0 + i < nch)
+        v[i] = *reinterpret_cast<const Row*>(o0 + ((c0 + i) * step + r1) * D + lane * PER);
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int c = c0 + i;
+      if (c < nch) {
+        const float wt = __shfl_sync(0xffffffffu, c < 32 ? wa : wb, c & 31);
+#pragma unroll
+        for (int e = 0; e < PER; ++e) acc[e] = fmaf(wt, static_cast<float>(v[i].e[e]), acc[e]);
+      }
+    }
+  }
+  const float inv = 1.f / w;
 #pragma unroll
   for (int e = 0; e < PER; e += 2)
     *reinterpret_cast<uint32_t*>(orow + e) = pack2<T>(acc[e] * inv, acc[e + 1] * inv);
-  if (lse != nullptr && lane == 0) lse[r1] = w > 0.f ? m + lg2(w) : -INFINITY;
+  if (lse != nullptr && lane == 0) lse[r1] = m + lg2(w);
 }
 
 }  // namespace pa

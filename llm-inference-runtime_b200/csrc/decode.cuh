@@ -439,6 +439,7 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
         // the same rule as pa_append_paged_kv_cache: the position must fall
         // inside the request's pages
         apos = __ldg(p.append_pos + cc.b);
+        if (p.append_pos_base != nullptr) apos -= __ldg(p.append_pos_base);
         if (apos < 0 || apos / kPage >= cc.n) {
           if (lane == 0) set_status(PA_ERR_DEVICE_CHECK);
           apos = -1;

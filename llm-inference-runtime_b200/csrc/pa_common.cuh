@@ -99,6 +99,9 @@ struct DecodeParams {
   // row (row b of new_k / new_v) goes to position append_pos[b] of its pages
   // before the attention reads that page. append_pos == nullptr: no append.
   const int32_t* append_pos;
+  // Optional device word subtracted from every append_pos entry (the cascade
+  // passes global positions; its level-1 pages start after the shared prefix).
+  const int32_t* append_pos_base;
   const uint8_t* new_k;
   const uint8_t* new_v;
   int64_t new_k_stride_n, new_k_stride_h, new_v_stride_n, new_v_stride_h;  // bytes

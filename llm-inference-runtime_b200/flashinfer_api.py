@@ -13,6 +13,8 @@ so ``models/llama.py`` works with ``import flashinfer`` pointed here:
 * ``BatchDecodeWithPagedKVCacheWrapper`` plan/begin_forward/run/forward
   (llama.py:62-67, 138, 236)
 * ``merge_state`` / ``merge_states`` / ``get_seq_lens`` (split-KV helpers)
+* ``MultiLevelCascadeAttentionWrapper`` (two levels: a prefix every request
+  shares, then each request's own pages) for radix-shared decode batches
 
 Every call goes through the C ABI (``_lib``) on the current torch CUDA
 stream. There is no CPU or PyTorch fallback: a missing library, an
@@ -615,6 +617,33 @@ class MultiLevelCascadeAttentionWrapper:
 
     def run(self, q: torch.Tensor, paged_kv_cache, out: Optional[torch.Tensor] = None,
             lse: Optional[torch.Tensor] = None, return_lse: bool = False):
+        return self._run(q, paged_kv_cache, None, out, lse, return_lse)
+
+    def run_with_append(self, q: torch.Tensor, paged_kv_cache, append_key: torch.Tensor,
+                        append_value: torch.Tensor, positions: torch.Tensor, *,
+                        out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                        return_lse: bool = False):
+        """This package's extension: the decode step's
+        ``append_paged_kv_cache(append_key, append_value, arange(B), positions, ...)``
+        (positions global, as get_batch_indices_positions gives them) fused
+        into the level-1 decode, then :meth:`run`'s levels and merge. Each
+        appended position must fall inside its request's own (level-1) pages;
+        the shared prefix pages are never written."""
+        desc = kv_cache_desc(paged_kv_cache, self._kv_layout)
+        if append_key.dtype != append_value.dtype or _dtype_code(append_key.dtype) != desc.dtype:
+            raise ValueError("append_key / append_value must have the KV cache's dtype")
+        for name, x in (("append_key", append_key), ("append_value", append_value)):
+            _row_strides(x, name)
+            if tuple(x.shape) != (self._batch, desc.num_kv_heads, desc.head_dim):
+                raise ValueError(f"{name} must be [{self._batch}, {desc.num_kv_heads}, "
+                                 f"{desc.head_dim}]")
+        positions = _i32_on(positions, q.device, "positions")
+        if positions.numel() != self._batch:
+            raise ValueError("positions must hold one entry per request")
+        return self._run(q, paged_kv_cache, (append_key, append_value, positions), out, lse,
+                         return_lse)
+
+    def _run(self, q, paged_kv_cache, append, out, lse, return_lse):
         if not self._planned:
             raise RuntimeError("plan() must be called before run()")
         desc = kv_cache_desc(paged_kv_cache, self._kv_layout)
@@ -632,12 +661,23 @@ class MultiLevelCascadeAttentionWrapper:
         if return_lse and lse is None:
             lse = torch.empty((self._batch, self._hq), dtype=torch.float32, device=q.device)
         scale = self._sm_scale if self._sm_scale is not None else 1.0 / math.sqrt(self._d)
-        _lib.check(_lib.load().pa_cascade_run(
-            _p(q), qsn, qsh, ctypes.byref(desc), _p(self._shared_indices), _p(self._indices),
-            _p(self._indptr), _p(self._last), self._batch, self._hq, float(scale), _p(self._ws),
-            self._ws.numel() * self._ws.element_size(), _p(out), _p(lse), _stream()),
-            "MultiLevelCascadeAttentionWrapper.run")
-        _after("MultiLevelCascadeAttentionWrapper.run")
+        ws_bytes = self._ws.numel() * self._ws.element_size()
+        if append is None:
+            _lib.check(_lib.load().pa_cascade_run(
+                _p(q), qsn, qsh, ctypes.byref(desc), _p(self._shared_indices), _p(self._indices),
+                _p(self._indptr), _p(self._last), self._batch, self._hq, float(scale),
+                _p(self._ws), ws_bytes, _p(out), _p(lse), _stream()),
+                "MultiLevelCascadeAttentionWrapper.run")
+            _after("MultiLevelCascadeAttentionWrapper.run")
+        else:
+            k, v, pos = append
+            _lib.check(_lib.load().pa_cascade_append_run(
+                _p(q), qsn, qsh, _p(k), k.stride(0), k.stride(1), _p(v), v.stride(0), v.stride(1),
+                _p(pos), ctypes.byref(desc), _p(self._shared_indices), _p(self._indices),
+                _p(self._indptr), _p(self._last), self._batch, self._hq, float(scale),
+                _p(self._ws), ws_bytes, _p(out), _p(lse), _stream()),
+                "MultiLevelCascadeAttentionWrapper.run_with_append")
+            _after("MultiLevelCascadeAttentionWrapper.run_with_append")
         return (out, lse) if return_lse else out
 
     forward = run

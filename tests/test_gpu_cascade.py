@@ -129,3 +129,69 @@ def test_cascade_rejects_unsupported_levels(fi):
         w.plan([two_groups, torch.arange(5, dtype=torch.int32)],
                [_t([0, 1, 2]), _t([0, 1, 2, 3, 4])], [_t([0, 1]), _t([2, 3, 4, 5])],
                [_t([16, 16]), _t([16] * 4)], 32, 4, 64, 16)
+
+
+def test_cascade_fused_append_matches_append_then_run(fi, workloads):
+    """run_with_append: the step's new K / V row lands in the request's own
+    pages (global position minus the prefix keys) before level 1 reads it.
+    The pool afterwards is bit-identical to append_paged_kv_cache + run, the
+    shared prefix pages are untouched, and the outputs agree."""
+    geom = workloads.LLAMA3_8B
+    hq, hkv, d = geom.num_qo_heads, geom.num_kv_heads, geom.head_dim
+    B, prefix = 24, 2048
+    prob = workloads.make_shared_prefix_problem(geom, B, prefix, 32, 256, seed=11)
+    sp = prefix // 16
+    levels = _split_tables(prob, sp)
+    pool_a = prob.pool[0].to(DEV)
+    pool_b = pool_a.clone()
+    seq = _t(prob.lengths)
+    k_new, v_new = prob.k_new.to(DEV), prob.v_new.to(DEV)
+    q = prob.q.to(DEV)
+    bi, pos = fi.get_batch_indices_positions(torch.arange(B + 1, dtype=torch.int32, device=DEV),
+                                             seq, B)
+    # reference order: append over the full tables, then the cascade
+    fi.append_paged_kv_cache(k_new, v_new, bi, pos, pool_a, _t(prob.kv_indices),
+                             _t(prob.kv_indptr), _t(prob.kv_last_page_len), kv_layout="HND")
+    want = _cascade(fi, q, pool_a, levels, hq, hkv, d)
+    sp_, si, sl, up, ui, ul = levels
+    ws = torch.empty(max(fi.cascade_workspace_bytes(B, hq, hkv, d), 1 << 20), dtype=torch.uint8,
+                     device=DEV)
+    w = fi.MultiLevelCascadeAttentionWrapper(2, ws, "HND")
+    w.plan([torch.tensor([0, B], dtype=torch.int32), torch.arange(B + 1, dtype=torch.int32)],
+           [_t(sp_), _t(up)], [_t(si), _t(ui)], [_t(sl), _t(ul)], hq, hkv, d, 16)
+    got = w.run_with_append(q, pool_b, k_new, v_new, pos)
+    torch.cuda.synchronize()
+    assert torch.equal(pool_a, pool_b)
+    assert torch.equal(pool_b[torch.as_tensor(si, dtype=torch.long, device=DEV)],
+                       prob.pool[0].to(DEV)[torch.as_tensor(si, dtype=torch.long, device=DEV)])
+    _check(got.cpu(), want.cpu().float())
+
+
+def test_cascade_fused_append_into_shared_page_is_reported(fi, lir, workloads):
+    """A position inside the shared prefix is a device-check error (the
+    prefix pages belong to every request), and nothing is written."""
+    import importlib
+    fa = importlib.import_module("llm-inference-runtime_b200.flashinfer_api")
+    geom = workloads.TINYLLAMA
+    hq, hkv, d = geom.num_qo_heads, geom.num_kv_heads, geom.head_dim
+    B = 4
+    prob = workloads.make_shared_prefix_problem(geom, B, 256, 32, 64, seed=3)
+    sp_, si, sl, up, ui, ul = _split_tables(prob, 16)
+    pool = prob.pool[0].to(DEV)
+    before = pool.clone()
+    ws = torch.empty(max(fi.cascade_workspace_bytes(B, hq, hkv, d), 1 << 20), dtype=torch.uint8,
+                     device=DEV)
+    w = fi.MultiLevelCascadeAttentionWrapper(2, ws, "HND")
+    w.plan([torch.tensor([0, B], dtype=torch.int32), torch.arange(B + 1, dtype=torch.int32)],
+           [_t(sp_), _t(up)], [_t(si), _t(ui)], [_t(sl), _t(ul)], hq, hkv, d, 16)
+    torch.cuda.synchronize()
+    lir._lib.device_status()
+    saved = fa._CHECK
+    fa._CHECK = False
+    try:
+        w.run_with_append(prob.q.to(DEV), pool, prob.k_new.to(DEV), prob.v_new.to(DEV),
+                          _t([100, 5, 255, 17]))  # all inside the 256-token prefix
+        assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
+    finally:
+        fa._CHECK = saved
+    assert torch.equal(pool, before)
