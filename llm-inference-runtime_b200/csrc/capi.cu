@@ -1011,6 +1011,7 @@ int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_la
   if (batch_size <= 0 || num_unique_indices < 0 || num_qo_heads <= 0 || num_kv_heads <= 0 ||
       num_qo_heads % num_kv_heads)
     return PA_ERR_INVALID_ARGUMENT;
+  if (num_qo_heads / num_kv_heads > kMaxGroup) return PA_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return PA_ERR_UNSUPPORTED;
   if (page_size != kPage) return PA_ERR_UNSUPPORTED;
   if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
@@ -1018,15 +1019,12 @@ int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_la
   if (!cascade_shape(current_device(), batch_size, num_qo_heads, num_kv_heads, head_dim, &sh))
     return PA_ERR_UNSUPPORTED;
   if (sh.L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int st = launch_chain(cascade_plan_kernel, dim3(1), dim3(256), 0, s, shared_kv_indptr,
-                        shared_kv_last_page_len, batch_size, num_qo_heads, num_kv_heads,
-                        head_dim, page_size, sh.qt, sh.max_chunks, ws, sh.L);
-  if (st != PA_OK) return st;
-  return pa_decode_plan(unique_kv_indptr, unique_kv_last_page_len, batch_size,
-                        num_unique_indices, num_qo_heads, num_kv_heads, head_dim, page_size,
-                        ws + sh.L.decode, sh.L.o0 - sh.L.decode, stream);
+  return launch_chain(cascade_plan_kernel, dim3(1), dim3(1024), 0,
+                      static_cast<cudaStream_t>(stream), shared_kv_indptr,
+                      shared_kv_last_page_len, unique_kv_indptr, unique_kv_last_page_len,
+                      num_unique_indices, batch_size, num_qo_heads, num_kv_heads, head_dim,
+                      page_size, sh.qt, sh.max_chunks, sh.dec.units, sh.dec.g.hb,
+                      static_cast<uint8_t*>(workspace), sh.L);
 }
 
 }  // extern "C"

@@ -84,11 +84,16 @@ __host__ __device__ inline CascadeWsLayout cascade_ws_layout(int batch, int hq, 
 // One CTA: validates the level-0 table ([0, n0] pages, last page length),
 // cuts the prefix into chunks of whole 128-key tiles and writes the chunk
 // tables, the prefill kernel's header and its work items (chunk, kv head,
-// query span).
+// query span); then plans level 1 (the decode plan over each request's own
+// pages) in the same launch.
 __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
-                                    const int32_t* __restrict__ shared_last, int batch, int hq,
-                                    int hkv, int head_dim, int page_size, int qt, int max_chunks,
-                                    uint8_t* __restrict__ ws, CascadeWsLayout L) {
+                                    const int32_t* __restrict__ shared_last,
+                                    const int32_t* __restrict__ unique_indptr,
+                                    const int32_t* __restrict__ unique_last,
+                                    int64_t num_unique_indices, int batch, int hq, int hkv,
+                                    int head_dim, int page_size, int qt, int max_chunks,
+                                    int decode_groups, int decode_hb, uint8_t* __restrict__ ws,
+                                    CascadeWsLayout L) {
   griddep_wait();
   griddep_launch_dependents();
   CascadeHeader* ch = reinterpret_cast<CascadeHeader*>(ws + L.hdr);
@@ -140,6 +145,9 @@ __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
     ch->magic = kCascadeMagic;
     if (bad) set_status(PA_ERR_DEVICE_CHECK);
   }
+  decode_plan_block(unique_indptr, unique_last, batch, hkv, hq, head_dim, page_size,
+                    num_unique_indices, decode_groups, decode_hb, /*min_per_group=*/4,
+                    ws + L.decode);
 }
 
 // One warp per (request, q head): log-sum-exp merge of the non-empty level-0

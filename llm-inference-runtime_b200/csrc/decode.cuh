@@ -40,12 +40,17 @@
 
 namespace pa {
 
-// Shared memory the decode rings may use per CTA (tunable at build time),
-// and the stage cap.
+// Shared memory the decode rings may use per CTA, per head size (tunable at
+// build time), and the stage cap.
 #ifndef PA_DECODE_RING_KB
 #define PA_DECODE_RING_KB 144
 #endif
-constexpr int kDecodeRingBudget = PA_DECODE_RING_KB * 1024;
+#ifndef PA_DECODE_RING_KB_D128
+#define PA_DECODE_RING_KB_D128 PA_DECODE_RING_KB
+#endif
+__host__ __device__ constexpr int decode_ring_budget(int head_dim) {
+  return (head_dim == 64 ? PA_DECODE_RING_KB : PA_DECODE_RING_KB_D128) * 1024;
+}
 constexpr int kDecodeMaxStages = 8;
 // Warps per CTA (one per kv head of each group). head_dim 128 pages are
 // 4x larger per head, so that kernel keeps 8 warps to fit >= 2 stages.
@@ -79,7 +84,7 @@ __host__ __device__ inline bool decode_geom(int hkv, int head_dim, DecodeGeom* g
   g->groups_per_cta = decode_cta_warps(head_dim) / hb;
   if (g->groups_per_cta < 1) return false;
   g->stage_bytes = hb * kPage * head_dim * 2 * 2;
-  int s = kDecodeRingBudget / (g->groups_per_cta * g->stage_bytes);
+  int s = decode_ring_budget(head_dim) / (g->groups_per_cta * g->stage_bytes);
   if (s > kDecodeMaxStages) s = kDecodeMaxStages;
   if (s < 2) return false;
   g->stages = s;
@@ -92,16 +97,14 @@ __host__ __device__ inline bool decode_geom(int hkv, int head_dim, DecodeGeom* g
 }
 
 // --------------------------------------------------------------------- plan
-// One CTA. Validates the CSR table, cuts the (request, head block, page)
-// stream into runs of Q pages for `num_groups` groups, clears the merge
-// counters.
-__global__ void decode_plan_kernel(const int32_t* __restrict__ kv_indptr,
-                                   const int32_t* __restrict__ last_len, int batch, int hkv,
-                                   int hq, int head_dim, int page_size, int64_t num_indices,
-                                   int num_groups, int hb, int min_per_group,
-                                   uint8_t* __restrict__ ws) {
-  griddep_wait();
-  griddep_launch_dependents();
+// One CTA (every thread calls it). Validates the CSR table, cuts the
+// (request, head block, page) stream into runs of Q pages for `num_groups`
+// groups, clears the merge counters.
+__device__ void decode_plan_block(const int32_t* __restrict__ kv_indptr,
+                                  const int32_t* __restrict__ last_len, int batch, int hkv,
+                                  int hq, int head_dim, int page_size, int64_t num_indices,
+                                  int num_groups, int hb, int min_per_group,
+                                  uint8_t* __restrict__ ws) {
   const DecodeWsLayout L = decode_ws_layout(num_groups, batch, hkv, head_dim, hb);
   DecodePlanHeader* hdr = reinterpret_cast<DecodePlanHeader*>(ws + L.hdr);
   int4* unit_start = reinterpret_cast<int4*>(ws + L.unit_start);
@@ -173,6 +176,17 @@ __global__ void decode_plan_kernel(const int32_t* __restrict__ kv_indptr,
   }
 }
 
+__global__ void decode_plan_kernel(const int32_t* __restrict__ kv_indptr,
+                                   const int32_t* __restrict__ last_len, int batch, int hkv,
+                                   int hq, int head_dim, int page_size, int64_t num_indices,
+                                   int num_groups, int hb, int min_per_group,
+                                   uint8_t* __restrict__ ws) {
+  griddep_wait();
+  griddep_launch_dependents();
+  decode_plan_block(kv_indptr, last_len, batch, hkv, hq, head_dim, page_size, num_indices,
+                    num_groups, hb, min_per_group, ws);
+}
+
 // ---------------------------------------------------------------------- run
 // Position in the work stream: request b, head block hblk, page j of n.
 struct StreamCursor {
@@ -198,9 +212,10 @@ __device__ __forceinline__ void cursor_next(StreamCursor& c, const int32_t* indp
 
 // Log-sum-exp merge of every piece of segment (request b, kv head `head`):
 // o = sum_u 2^(lse_u - max) o_u / sum_u 2^(lse_u - max). The G x D outputs
-// are spread over the lanes in float4 granules; each granule streams its
-// pieces' LSEs and partial rows with independent loads (online max), so a
-// merge costs a couple of L2 round trips rather than one per row.
+// are spread over the lanes in float4 granules, kItems granules per lane at
+// a time; the LSEs and partial rows of kBatch pieces of all of them are
+// loaded together (online max), so a segment of up to kBatch pieces costs
+// one L2 round trip rather than one per granule or per piece.
 template <typename T, int D>
 __device__ __noinline__ void merge_segment(const float* part_lse, const float* part_o, T* out,
                                            float* lse, int* counter, int G, int hq, int hkv,
@@ -209,46 +224,66 @@ __device__ __noinline__ void merge_segment(const float* part_lse, const float* p
   const int u0 = seg_start / Q, u1 = (seg_start + seg_len - 1) / Q;
   T* ob = out + (static_cast<size_t>(b) * hq + head * G) * D;
   constexpr int C4 = D / 4;
-  for (int it = lane; it < G * C4; it += 32) {
-    const int r = it / C4, c = (it - r * C4) * 4;
-    float m = -INFINITY, w = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    // pieces in batches of 4: all loads of a batch are in flight together,
-    // so a segment of n pieces costs ceil(n / 4) L2 round trips
-    constexpr int kBatch = 4;
-    for (int u = u0; u <= u1; u += kBatch) {
-      float lb[kBatch];
-      float4 vb[kBatch];
+  constexpr int kItems = 4;
+  constexpr int kBatch = 4;
+  const int n_items = G * C4;
+  for (int it0 = 0; it0 < n_items; it0 += 32 * kItems) {
+    float m[kItems], w[kItems];
+    float4 acc[kItems];
 #pragma unroll
-      for (int k = 0; k < kBatch; ++k) {
-        lb[k] = -INFINITY;
-        vb[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (u + k <= u1) {
-          const int uk = u + k;
-          const size_t sl = static_cast<size_t>((uk * 2 + (seg_start <= uk * Q ? 0 : 1)) * HB + hh);
-          lb[k] = __ldcg(part_lse + sl * kMaxGroup + r);
-          vb[k] = __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
+    for (int j = 0; j < kItems; ++j) {
+      m[j] = -INFINITY;
+      w[j] = 0.f;
+      acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int u = u0; u <= u1; u += kBatch) {
+      float lb[kItems][kBatch];
+      float4 vb[kItems][kBatch];
+#pragma unroll
+      for (int j = 0; j < kItems; ++j) {
+        const int it = it0 + j * 32 + lane;
+        const int r = it / C4, c = (it - r * C4) * 4;
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+          lb[j][k] = -INFINITY;
+          vb[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (it < n_items && u + k <= u1) {
+            const int uk = u + k;
+            const size_t sl = static_cast<size_t>((uk * 2 + (seg_start <= uk * Q ? 0 : 1)) * HB + hh);
+            lb[j][k] = __ldcg(part_lse + sl * kMaxGroup + r);
+            vb[j][k] = __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
+          }
         }
       }
 #pragma unroll
-      for (int k = 0; k < kBatch; ++k) {
-        if (u + k > u1) break;
-        const float mn = fmaxf(m, lb[k]);
-        const float sc = ex2(m - mn), wt = ex2(lb[k] - mn);
-        acc.x = acc.x * sc + wt * vb[k].x;
-        acc.y = acc.y * sc + wt * vb[k].y;
-        acc.z = acc.z * sc + wt * vb[k].z;
-        acc.w = acc.w * sc + wt * vb[k].w;
-        w = w * sc + wt;
-        m = mn;
+      for (int j = 0; j < kItems; ++j) {
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+          if (u + k > u1) break;
+          const float mn = fmaxf(m[j], lb[j][k]);
+          const float sc = ex2(m[j] - mn), wt = ex2(lb[j][k] - mn);
+          acc[j].x = acc[j].x * sc + wt * vb[j][k].x;
+          acc[j].y = acc[j].y * sc + wt * vb[j][k].y;
+          acc[j].z = acc[j].z * sc + wt * vb[j][k].z;
+          acc[j].w = acc[j].w * sc + wt * vb[j][k].w;
+          w[j] = w[j] * sc + wt;
+          m[j] = mn;
+        }
       }
     }
-    const float inv = 1.f / w;
-    uint2 packed;
-    packed.x = pack2<T>(acc.x * inv, acc.y * inv);
-    packed.y = pack2<T>(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(ob + r * D + c) = packed;
-    if (lse != nullptr && c == 0) lse[static_cast<size_t>(b) * hq + head * G + r] = m + lg2(w);
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      const int it = it0 + j * 32 + lane;
+      if (it >= n_items) continue;
+      const int r = it / C4, c = (it - r * C4) * 4;
+      const float inv = 1.f / w[j];
+      uint2 packed;
+      packed.x = pack2<T>(acc[j].x * inv, acc[j].y * inv);
+      packed.y = pack2<T>(acc[j].z * inv, acc[j].w * inv);
+      *reinterpret_cast<uint2*>(ob + r * D + c) = packed;
+      if (lse != nullptr && c == 0)
+        lse[static_cast<size_t>(b) * hq + head * G + r] = m[j] + lg2(w[j]);
+    }
   }
   __syncwarp();
   if (lane == 0) counter[b * hkv + head] = 0;  // ready for the next launch
@@ -293,6 +328,9 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   // everything above is private to this CTA; from here on the plan and the
   // pool (which the previous kernel may have written) are read
   griddep_wait();
+  // this group's start, loaded alongside the header (the workspace is sized
+  // for this grid, so the load is in bounds whatever the header holds)
+  const int4 st = p.unit_start[grp];
 
   if (hdr->magic != kDecodeMagic || hdr->num_units != num_groups ||
       hdr->batch_size != p.batch_size || hdr->num_kv_heads != p.num_kv_heads ||
@@ -325,7 +363,6 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   int* rel = relc + g_local * S;
   int* walk = walk_all + warp * 2 * (S + 1);
 
-  const int4 st = p.unit_start[grp];
   StreamCursor pc;
   pc.b = st.x;
   pc.hblk = st.y;
@@ -666,14 +703,17 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   griddep_launch_dependents();
 
   if (n_pend > 0) {
-    // Publish this warp's partials, then count its pieces; the warp that
-    // completes a segment's count merges that segment.
+    // Publish this warp's partials, then count its pieces (both counts in
+    // flight together); the warp that completes a segment's count merges it.
     __threadfence();
     __syncwarp();
+    int old0 = 0, old1 = 0;
+    if (lane == 0) {
+      old0 = atomicAdd(p.counter + pend_b[0] * hkv + pend_head[0], 1);
+      if (n_pend > 1) old1 = atomicAdd(p.counter + pend_b[1] * hkv + pend_head[1], 1);
+    }
     for (int k = 0; k < n_pend; ++k) {
-      int old = 0;
-      if (lane == 0) old = atomicAdd(p.counter + pend_b[k] * hkv + pend_head[k], 1);
-      old = __shfl_sync(0xffffffffu, old, 0);
+      const int old = __shfl_sync(0xffffffffu, k == 0 ? old0 : old1, 0);
       const int u0 = pend_seg[k] / Q, u1 = (pend_seg[k] + pend_len[k] - 1) / Q;
       if (old == u1 - u0) {
         __threadfence();

@@ -195,3 +195,36 @@ def test_cascade_fused_append_into_shared_page_is_reported(fi, lir, workloads):
     finally:
         fa._CHECK = saved
     assert torch.equal(pool, before)
+
+
+@pytest.mark.parametrize("geom_name,dtype", [("TINYLLAMA", torch.float16), ("LLAMA3_8B", torch.float16),
+                                             ("LLAMA3_8B", torch.bfloat16)])
+def test_cascade_nhd_layout_strided_q_fp16(fi, workloads, geom_name, dtype):
+    """The NHD pool layout ([N, 2, P, H, D]), fp16, and q as a strided view
+    of a fused QKV row (as the patched attention passes it), against the
+    plain decode over the full tables on the same pool."""
+    geom = getattr(workloads, geom_name)
+    hq, hkv, d = geom.num_qo_heads, geom.num_kv_heads, geom.head_dim
+    B, prefix = 19, 768
+    prob = workloads.make_shared_prefix_problem(geom, B, prefix, 1, 90, seed=23, dtype=dtype)
+    sp_, si, sl, up, ui, ul = _split_tables(prob, prefix // 16)
+    nhd = prob.pool[0].permute(0, 1, 3, 2, 4).contiguous().to(DEV)  # [N, 2, P, H, D]
+    qkv = torch.randn(B, (hq + 2 * hkv) * d, dtype=dtype, device=DEV)
+    q = qkv[:, :hq * d].view(B, hq, d)
+    q.copy_(prob.q.to(DEV))
+    assert not q.is_contiguous()
+    ws = torch.empty(max(fi.cascade_workspace_bytes(B, hq, hkv, d), 1 << 20), dtype=torch.uint8,
+                     device=DEV)
+    w = fi.MultiLevelCascadeAttentionWrapper(2, ws, "NHD")
+    w.plan([torch.tensor([0, B], dtype=torch.int32), torch.arange(B + 1, dtype=torch.int32)],
+           [_t(sp_), _t(up)], [_t(si), _t(ui)], [_t(sl), _t(ul)], hq, hkv, d, 16)
+    got = w.run(q, nhd)
+    pw = fi.BatchDecodeWithPagedKVCacheWrapper(torch.empty(128 << 20, dtype=torch.uint8,
+                                                           device=DEV), "NHD")
+    pw.plan(_t(prob.kv_indptr), _t(prob.kv_indices), _t(prob.kv_last_page_len), hq, hkv, d, 16,
+            q_data_type=dtype)
+    plain = pw.run(q, nhd)
+    _check(got.float().cpu(), plain.float().cpu())
+    want, _ = attention.decode(prob.q.float(), prob.pool[0].float(), prob.kv_indptr,
+                               prob.kv_indices, prob.kv_last_page_len, requests=[0, 7, 18])
+    _check(got.float().cpu()[[0, 7, 18]], want[[0, 7, 18]])
