@@ -210,83 +210,108 @@ __device__ __forceinline__ void cursor_next(StreamCursor& c, const int32_t* indp
   } while (c.n == 0);
 }
 
-// Log-sum-exp merge of every piece of segment (request b, kv head `head`):
-// o = sum_u 2^(lse_u - max) o_u / sum_u 2^(lse_u - max). The G x D outputs
-// are spread over the lanes in float4 granules, kItems granules per lane at
-// a time; the LSEs and partial rows of kBatch pieces of all of them are
-// loaded together (online max), so a segment of up to kBatch pieces costs
-// one L2 round trip rather than one per granule or per piece.
+// A split segment (request b, kv head `head`) whose pieces one warp merges.
+struct MergeSeg {
+  int b, head, seg_start, seg_len;
+};
+
+// Log-sum-exp merge of every piece of up to two segments (the two a warp's
+// run can end pieces of): o = sum_u 2^(lse_u - max) o_u / sum_u 2^(lse_u -
+// max). The G x D outputs are spread over the lanes in float4 granules,
+// kItems granules per lane at a time; the LSEs and partial rows of kBatch
+// pieces of every granule of both segments are loaded together (online
+// max), so merging both segments costs one L2 round trip per kBatch pieces
+// rather than one per granule, piece or segment.
 template <typename T, int D>
-__device__ __noinline__ void merge_segment(const float* part_lse, const float* part_o, T* out,
-                                           float* lse, int* counter, int G, int hq, int hkv,
-                                           int Q, int HB, int hh, int b, int head, int seg_start,
-                                           int seg_len, int lane) {
-  const int u0 = seg_start / Q, u1 = (seg_start + seg_len - 1) / Q;
-  T* ob = out + (static_cast<size_t>(b) * hq + head * G) * D;
+__device__ __noinline__ void merge_segments(const float* part_lse, const float* part_o, T* out,
+                                            float* lse, int* counter, int G, int hq, int hkv,
+                                            int Q, int HB, int hh, MergeSeg sa, MergeSeg sb,
+                                            int nseg, int lane) {
   constexpr int C4 = D / 4;
   constexpr int kItems = 4;
-  constexpr int kBatch = 4;
+  constexpr int kBatch = 2;
   const int n_items = G * C4;
-  for (int it0 = 0; it0 < n_items; it0 += 32 * kItems) {
-    float m[kItems], w[kItems];
-    float4 acc[kItems];
+  const MergeSeg seg[2] = {sa, sb};
+  int u0[2], np[2];
 #pragma unroll
-    for (int j = 0; j < kItems; ++j) {
-      m[j] = -INFINITY;
-      w[j] = 0.f;
-      acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < 2; ++s) {
+    u0[s] = seg[s].seg_start / Q;
+    np[s] = s < nseg ? (seg[s].seg_start + seg[s].seg_len - 1) / Q - u0[s] + 1 : 0;
+  }
+  const int np_max = max(np[0], np[1]);
+  for (int it0 = 0; it0 < n_items; it0 += 32 * kItems) {
+    float m[2][kItems], w[2][kItems];
+    float4 acc[2][kItems];
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int j = 0; j < kItems; ++j) {
+        m[s][j] = -INFINITY;
+        w[s][j] = 0.f;
+        acc[s][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    for (int ub = 0; ub < np_max; ub += kBatch) {
+      float lb[2][kItems][kBatch];
+      float4 vb[2][kItems][kBatch];
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int j = 0; j < kItems; ++j) {
+          const int it = it0 + j * 32 + lane;
+          const int r = it / C4, c = (it - r * C4) * 4;
+#pragma unroll
+          for (int k = 0; k < kBatch; ++k) {
+            lb[s][j][k] = -INFINITY;
+            vb[s][j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (it < n_items && ub + k < np[s]) {
+              const int uk = u0[s] + ub + k;
+              const size_t sl =
+                  static_cast<size_t>((uk * 2 + (seg[s].seg_start <= uk * Q ? 0 : 1)) * HB + hh);
+              lb[s][j][k] = __ldcg(part_lse + sl * kMaxGroup + r);
+              vb[s][j][k] =
+                  __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
+            }
+          }
+        }
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int j = 0; j < kItems; ++j)
+#pragma unroll
+          for (int k = 0; k < kBatch; ++k) {
+            if (ub + k >= np[s]) break;
+            const float mn = fmaxf(m[s][j], lb[s][j][k]);
+            const float sc = ex2(m[s][j] - mn), wt = ex2(lb[s][j][k] - mn);
+            acc[s][j].x = acc[s][j].x * sc + wt * vb[s][j][k].x;
+            acc[s][j].y = acc[s][j].y * sc + wt * vb[s][j][k].y;
+            acc[s][j].z = acc[s][j].z * sc + wt * vb[s][j][k].z;
+            acc[s][j].w = acc[s][j].w * sc + wt * vb[s][j][k].w;
+            w[s][j] = w[s][j] * sc + wt;
+            m[s][j] = mn;
+          }
     }
-    for (int u = u0; u <= u1; u += kBatch) {
-      float lb[kItems][kBatch];
-      float4 vb[kItems][kBatch];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      if (s >= nseg) break;
+      T* ob = out + (static_cast<size_t>(seg[s].b) * hq + seg[s].head * G) * D;
 #pragma unroll
       for (int j = 0; j < kItems; ++j) {
         const int it = it0 + j * 32 + lane;
+        if (it >= n_items) continue;
         const int r = it / C4, c = (it - r * C4) * 4;
-#pragma unroll
-        for (int k = 0; k < kBatch; ++k) {
-          lb[j][k] = -INFINITY;
-          vb[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (it < n_items && u + k <= u1) {
-            const int uk = u + k;
-            const size_t sl = static_cast<size_t>((uk * 2 + (seg_start <= uk * Q ? 0 : 1)) * HB + hh);
-            lb[j][k] = __ldcg(part_lse + sl * kMaxGroup + r);
-            vb[j][k] = __ldcg(reinterpret_cast<const float4*>(part_o + (sl * kMaxGroup + r) * D + c));
-          }
-        }
+        const float inv = 1.f / w[s][j];
+        uint2 packed;
+        packed.x = pack2<T>(acc[s][j].x * inv, acc[s][j].y * inv);
+        packed.y = pack2<T>(acc[s][j].z * inv, acc[s][j].w * inv);
+        *reinterpret_cast<uint2*>(ob + r * D + c) = packed;
+        if (lse != nullptr && c == 0)
+          lse[static_cast<size_t>(seg[s].b) * hq + seg[s].head * G + r] = m[s][j] + lg2(w[s][j]);
       }
-#pragma unroll
-      for (int j = 0; j < kItems; ++j) {
-#pragma unroll
-        for (int k = 0; k < kBatch; ++k) {
-          if (u + k > u1) break;
-          const float mn = fmaxf(m[j], lb[j][k]);
-          const float sc = ex2(m[j] - mn), wt = ex2(lb[j][k] - mn);
-          acc[j].x = acc[j].x * sc + wt * vb[j][k].x;
-          acc[j].y = acc[j].y * sc + wt * vb[j][k].y;
-          acc[j].z = acc[j].z * sc + wt * vb[j][k].z;
-          acc[j].w = acc[j].w * sc + wt * vb[j][k].w;
-          w[j] = w[j] * sc + wt;
-          m[j] = mn;
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kItems; ++j) {
-      const int it = it0 + j * 32 + lane;
-      if (it >= n_items) continue;
-      const int r = it / C4, c = (it - r * C4) * 4;
-      const float inv = 1.f / w[j];
-      uint2 packed;
-      packed.x = pack2<T>(acc[j].x * inv, acc[j].y * inv);
-      packed.y = pack2<T>(acc[j].z * inv, acc[j].w * inv);
-      *reinterpret_cast<uint2*>(ob + r * D + c) = packed;
-      if (lse != nullptr && c == 0)
-        lse[static_cast<size_t>(b) * hq + head * G + r] = m[j] + lg2(w[j]);
     }
   }
   __syncwarp();
-  if (lane == 0) counter[b * hkv + head] = 0;  // ready for the next launch
+  if (lane == 0)  // ready for the next launch
+    for (int s = 0; s < nseg; ++s) counter[seg[s].b * hkv + seg[s].head] = 0;
 }
 
 template <typename T, int D>
@@ -704,7 +729,8 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
 
   if (n_pend > 0) {
     // Publish this warp's partials, then count its pieces (both counts in
-    // flight together); the warp that completes a segment's count merges it.
+    // flight together); the warp that completes a segment's count merges it,
+    // both segments in one pass when it completes both.
     __threadfence();
     __syncwarp();
     int old0 = 0, old1 = 0;
@@ -712,14 +738,16 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
       old0 = atomicAdd(p.counter + pend_b[0] * hkv + pend_head[0], 1);
       if (n_pend > 1) old1 = atomicAdd(p.counter + pend_b[1] * hkv + pend_head[1], 1);
     }
-    for (int k = 0; k < n_pend; ++k) {
-      const int old = __shfl_sync(0xffffffffu, k == 0 ? old0 : old1, 0);
-      const int u0 = pend_seg[k] / Q, u1 = (pend_seg[k] + pend_len[k] - 1) / Q;
-      if (old == u1 - u0) {
-        __threadfence();
-        merge_segment<T, D>(p.part_lse, p.part_o, out, p.lse, p.counter, G, hq, hkv, Q, HB, hh,
-                            pend_b[k], pend_head[k], pend_seg[k], pend_len[k], lane);
-      }
+    old0 = __shfl_sync(0xffffffffu, old0, 0);
+    old1 = __shfl_sync(0xffffffffu, old1, 0);
+    const bool last0 = old0 == (pend_seg[0] + pend_len[0] - 1) / Q - pend_seg[0] / Q;
+    const bool last1 = n_pend > 1 && old1 == (pend_seg[1] + pend_len[1] - 1) / Q - pend_seg[1] / Q;
+    if (last0 || last1) {
+      const MergeSeg s0{pend_b[0], pend_head[0], pend_seg[0], pend_len[0]};
+      const MergeSeg s1{pend_b[1], pend_head[1], pend_seg[1], pend_len[1]};
+      __threadfence();
+      merge_segments<T, D>(p.part_lse, p.part_o, out, p.lse, p.counter, G, hq, hkv, Q, HB, hh,
+                           last0 ? s0 : s1, s1, last0 && last1 ? 2 : 1, lane);
     }
   }
 }
