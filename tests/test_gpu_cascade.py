@@ -232,3 +232,21 @@ def test_cascade_nhd_layout_strided_q_fp16(fi, workloads, geom_name, dtype):
     want, _ = attention.decode(prob.q.float(), prob.pool[0].float(), prob.kv_indptr,
                                prob.kv_indices, prob.kv_last_page_len, requests=[0, 7, 18])
     _check(got.float().cpu()[[0, 7, 18]], want[[0, 7, 18]])
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(8, 8, 128), (16, 8, 64), (32, 2, 128), (64, 4, 64)])
+def test_cascade_gqa_groups(fi, workloads, hq, hkv, d):
+    """GQA groups 1, 2 and 16 at both head sizes: the level-0 tiles pack
+    128 / g queries x g heads per kv head, level 1 puts the g heads in one
+    decode tile; both against the plain decode and the oracle."""
+    geom = workloads.Geometry(num_qo_heads=hq, num_kv_heads=hkv, head_dim=d)
+    B, prefix = 11, 1024
+    prob = workloads.make_shared_prefix_problem(geom, B, prefix, 1, 200, seed=hq * 10 + hkv)
+    levels = _split_tables(prob, prefix // 16)
+    got = _cascade(fi, prob.q, prob.pool[0], levels, hq, hkv, d)
+    plain = _plain(fi, prob, hq, hkv, d)
+    _check(got.cpu(), plain.cpu().float())
+    sample = [0, 5, 10]
+    want, _ = attention.decode(prob.q, prob.pool[0].float(), prob.kv_indptr, prob.kv_indices,
+                               prob.kv_last_page_len, requests=sample)
+    _check(got.cpu()[sample], want[sample])
