@@ -260,3 +260,34 @@ def test_attention_oracle_matches_flashinfer_on_b200(case):
                                    layout=case["layout"])
     mx, mean, ok = attention.compare(want, got)
     assert ok, f"max-abs {mx:.3e} mean-abs {mean:.3e}"
+
+
+def test_two_level_merge_equals_concatenated_tables():
+    """The expected value the GPU cascade tests build — decode over the
+    shared prefix pages and over each request's own pages separately, merged
+    by base-2 log-sum-exp with a level of LSE -inf contributing nothing —
+    equals the oracle decode over the concatenated tables (full shared pages;
+    requests with no pages of their own included)."""
+    g = torch.Generator().manual_seed(3)
+    B, H, HKV, D, N = 5, 8, 2, 16, 40
+    pool = torch.randn(N, 2, HKV, 16, D, generator=g)
+    q = torch.randn(B, H, D, generator=g)
+    perm = torch.randperm(N, generator=g).numpy().astype(np.int32)
+    shared = perm[:3]
+    counts = np.array([2, 0, 1, 3, 0])
+    up = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    ui = perm[3:3 + up[-1]]
+    ul = np.array([5, 16, 16, 1, 16], dtype=np.int32)
+    o0, l0 = attention.decode(q, pool, np.arange(B + 1) * 3, np.tile(shared, B), np.full(B, 16))
+    o1, l1 = attention.decode(q, pool, up, ui, ul)
+    m = torch.maximum(l0, l1)
+    m = torch.where(torch.isinf(m), torch.zeros_like(m), m)
+    w0, w1 = torch.exp2(l0 - m), torch.exp2(l1 - m)
+    merged = (o0 * w0[..., None] + o1 * w1[..., None]) / (w0 + w1)[..., None]
+    full_ptr = np.concatenate([[0], np.cumsum(3 + counts)]).astype(np.int32)
+    full_idx = np.concatenate([np.concatenate([shared, ui[up[b]:up[b + 1]]]) for b in range(B)])
+    full_last = np.where(counts > 0, ul, 16).astype(np.int32)
+    want, want_lse = attention.decode(q, pool, full_ptr, full_idx, full_last)
+    assert torch.allclose(merged, want, atol=1e-5)
+    lse = m + torch.log2(w0 + w1)
+    assert torch.allclose(lse, want_lse, atol=1e-5)
