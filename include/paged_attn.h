@@ -268,7 +268,9 @@ int pa_decode_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
  * request's full table (src/models/llama.py:230-245), reading the prefix
  * once per request; here it is attended once for all requests.
  *   level 0: shared_kv_indptr = {0, n0}, shared_kv_indices[n0],
- *            shared_kv_last_page_len[1] — the prefix pages;
+ *            shared_kv_last_page_len[1] — the prefix pages (the plan is
+ *            given num_shared_indices, the page ids the array holds; n0
+ *            beyond it is a device-check error);
  *   level 1: unique_kv_indptr[B+1], unique_kv_indices,
  *            unique_kv_last_page_len[B] — each request's pages after it
  *            (a request may have none).
@@ -278,10 +280,11 @@ int pa_decode_append_run(const void* q, int64_t q_stride_n, int64_t q_stride_h,
 size_t pa_cascade_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads,
                                   int32_t head_dim);
 int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_last_page_len,
-                    const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
-                    int32_t batch_size, int64_t num_unique_indices, int32_t num_qo_heads,
-                    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, void* workspace,
-                    size_t workspace_bytes, void* stream);
+                    int64_t num_shared_indices, const int32_t* unique_kv_indptr,
+                    const int32_t* unique_kv_last_page_len, int32_t batch_size,
+                    int64_t num_unique_indices, int32_t num_qo_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
+                    void* stream);
 int pa_cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_kv_cache* cache,
                    const int32_t* shared_kv_indices, const int32_t* unique_kv_indices,
                    const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,

@@ -117,8 +117,8 @@ SIGNATURES = {
     "pa_cascade_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),
     "pa_cascade_plan": (
         c_int32,
-        [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32,
-         c_int32, c_void_p, c_size_t, c_void_p],
+        [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_int32,
+         c_int32, c_int32, c_void_p, c_size_t, c_void_p],
     ),
     "pa_cascade_run": (
         c_int32,

@@ -1007,15 +1007,16 @@ size_t pa_cascade_workspace_bytes(int32_t batch_size, int32_t num_qo_heads, int3
 }
 
 int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_last_page_len,
-                    const int32_t* unique_kv_indptr, const int32_t* unique_kv_last_page_len,
-                    int32_t batch_size, int64_t num_unique_indices, int32_t num_qo_heads,
-                    int32_t num_kv_heads, int32_t head_dim, int32_t page_size, void* workspace,
-                    size_t workspace_bytes, void* stream) {
+                    int64_t num_shared_indices, const int32_t* unique_kv_indptr,
+                    const int32_t* unique_kv_last_page_len, int32_t batch_size,
+                    int64_t num_unique_indices, int32_t num_qo_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int32_t page_size, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   if (shared_kv_indptr == nullptr || shared_kv_last_page_len == nullptr ||
       unique_kv_indptr == nullptr || unique_kv_last_page_len == nullptr || workspace == nullptr)
     return PA_ERR_INVALID_ARGUMENT;
-  if (batch_size <= 0 || num_unique_indices < 0 || num_qo_heads <= 0 || num_kv_heads <= 0 ||
-      num_qo_heads % num_kv_heads)
+  if (batch_size <= 0 || num_unique_indices < 0 || num_shared_indices < 0 || num_qo_heads <= 0 ||
+      num_kv_heads <= 0 || num_qo_heads % num_kv_heads)
     return PA_ERR_INVALID_ARGUMENT;
   if (num_qo_heads / num_kv_heads > kMaxGroup) return PA_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128) return PA_ERR_UNSUPPORTED;
@@ -1027,7 +1028,8 @@ int pa_cascade_plan(const int32_t* shared_kv_indptr, const int32_t* shared_kv_la
   if (sh.L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
   return launch_chain(cascade_plan_kernel, dim3(1), dim3(1024), 0,
                       static_cast<cudaStream_t>(stream), shared_kv_indptr,
-                      shared_kv_last_page_len, unique_kv_indptr, unique_kv_last_page_len,
+                      shared_kv_last_page_len, num_shared_indices, unique_kv_indptr,
+                      unique_kv_last_page_len,
                       num_unique_indices, batch_size, num_qo_heads, num_kv_heads, head_dim,
                       page_size, sh.qt, sh.max_chunks, sh.dec.units, sh.dec.g.hb,
                       static_cast<uint8_t*>(workspace), sh.L);

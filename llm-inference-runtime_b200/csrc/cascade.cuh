@@ -81,13 +81,15 @@ __host__ __device__ inline CascadeWsLayout cascade_ws_layout(int batch, int hq, 
   return L;
 }
 
-// One CTA: validates the level-0 table ([0, n0] pages, last page length),
+// One CTA: validates the level-0 table ([0, n0] pages within the
+// num_shared_indices page ids given, last page length),
 // cuts the prefix into chunks of whole 128-key tiles and writes the chunk
 // tables, the prefill kernel's header and its work items (chunk, kv head,
 // query span); then plans level 1 (the decode plan over each request's own
 // pages) in the same launch.
 __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
                                     const int32_t* __restrict__ shared_last,
+                                    int64_t num_shared_indices,
                                     const int32_t* __restrict__ unique_indptr,
                                     const int32_t* __restrict__ unique_last,
                                     int64_t num_unique_indices, int batch, int hq, int hkv,
@@ -107,7 +109,8 @@ __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
 
   const int n0 = shared_indptr[1] - shared_indptr[0];
   const int lp = n0 > 0 ? shared_last[0] : page_size;
-  const bool bad = shared_indptr[0] != 0 || n0 < 0 || lp < 1 || lp > page_size;
+  const bool bad = shared_indptr[0] != 0 || n0 < 0 || n0 > num_shared_indices || lp < 1 ||
+                   lp > page_size;
   const int tile_pages = kPfKeys / page_size;
   int ppc = n0 > 0 ? (n0 + max_chunks - 1) / max_chunks : tile_pages;
   ppc = (ppc + tile_pages - 1) / tile_pages * tile_pages;  // whole key tiles per chunk

@@ -608,8 +608,9 @@ class MultiLevelCascadeAttentionWrapper:
                                                              head_dim, page_size)
         self._sm_scale = sm_scale
         _lib.check(_lib.load().pa_cascade_plan(
-            _p(self._shared_indptr), _p(self._shared_last), _p(self._indptr), _p(self._last),
-            batch, self._indices.numel(), num_qo_heads, num_kv_heads, head_dim, page_size,
+            _p(self._shared_indptr), _p(self._shared_last), self._shared_indices.numel(),
+            _p(self._indptr), _p(self._last), batch, self._indices.numel(), num_qo_heads,
+            num_kv_heads, head_dim, page_size,
             _p(self._ws), self._ws.numel() * self._ws.element_size(), _stream()),
             "MultiLevelCascadeAttentionWrapper.plan")
         _after("MultiLevelCascadeAttentionWrapper.plan")

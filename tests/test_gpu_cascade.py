@@ -250,3 +250,31 @@ def test_cascade_gqa_groups(fi, workloads, hq, hkv, d):
     want, _ = attention.decode(prob.q, prob.pool[0].float(), prob.kv_indptr, prob.kv_indices,
                                prob.kv_last_page_len, requests=sample)
     _check(got.cpu()[sample], want[sample])
+
+
+def test_cascade_prefix_table_past_its_page_ids_is_reported(fi, lir, workloads):
+    """A level-0 table that names more pages than the shared index array
+    holds is a device-check error from the plan; no kernel reads past the
+    array (the level-0 work list is left empty)."""
+    import importlib
+    fa = importlib.import_module("llm-inference-runtime_b200.flashinfer_api")
+    geom = workloads.TINYLLAMA
+    hq, hkv, d = geom.num_qo_heads, geom.num_kv_heads, geom.head_dim
+    B = 4
+    prob = workloads.make_shared_prefix_problem(geom, B, 256, 32, 64, seed=5)
+    sp_, si, sl, up, ui, ul = _split_tables(prob, 16)
+    ws = torch.empty(max(fi.cascade_workspace_bytes(B, hq, hkv, d), 1 << 20), dtype=torch.uint8,
+                     device=DEV)
+    w = fi.MultiLevelCascadeAttentionWrapper(2, ws, "HND")
+    torch.cuda.synchronize()
+    lir._lib.device_status()
+    saved = fa._CHECK
+    fa._CHECK = False
+    try:
+        # 16 pages named, 5 page ids given
+        w.plan([torch.tensor([0, B], dtype=torch.int32), torch.arange(B + 1, dtype=torch.int32)],
+               [_t([0, 16]), _t(up)], [_t(si[:5]), _t(ui)], [_t(sl), _t(ul)], hq, hkv, d, 16)
+        w.run(prob.q.to(DEV), prob.pool[0].to(DEV))
+        assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
+    finally:
+        fa._CHECK = saved
