@@ -92,14 +92,15 @@ int pa_batch_indices_positions(const int32_t* append_indptr, const int32_t* seq_
  * [nnz, H_kv, D] (strides in elements, last dim contiguous) into the pool:
  *   page = kv_indices[kv_indptr[b] + pos / P], slot = pos % P,
  *   with b = batch_indices[t], pos = positions[t].
- * Rows whose page falls outside the request's pages or the pool are skipped
- * and reported as PA_ERR_DEVICE_CHECK. Bit-exact copy. */
+ * kv_indices holds num_kv_indices page ids; a kv_indptr range outside them,
+ * or a page outside the request's pages or the pool, skips the row and
+ * reports PA_ERR_DEVICE_CHECK. Bit-exact copy. */
 int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64_t key_stride_h,
                              const void* append_value, int64_t value_stride_n,
                              int64_t value_stride_h, const int32_t* batch_indices,
                              const int32_t* positions, int32_t nnz, const pa_kv_cache* cache,
-                             const int32_t* kv_indices, const int32_t* kv_indptr,
-                             int32_t batch_size, void* stream);
+                             const int32_t* kv_indices, int64_t num_kv_indices,
+                             const int32_t* kv_indptr, int32_t batch_size, void* stream);
 
 /* Replaces flashinfer.apply_rope_pos_ids_inplace(q, k, pos_ids,
  * rotary_dim, interleave, rope_scale, rope_theta) (src/models/llama.py:175-182).
@@ -127,7 +128,8 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
                          const int32_t* positions, int32_t nnz, int32_t num_qo_heads,
                          int32_t rotary_dim, int32_t interleave, float rope_scale,
                          float rope_theta, const pa_kv_cache* cache, const int32_t* kv_indices,
-                         const int32_t* kv_indptr, int32_t batch_size, void* stream);
+                         int64_t num_kv_indices, const int32_t* kv_indptr, int32_t batch_size,
+                         void* stream);
 
 /* Replaces the Python table build of StepExecutor._run_decode
  * (src/engine/runtime/step_executor.py:204-225) with a device build:
@@ -203,7 +205,8 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
                        int64_t q_stride_n, const int32_t* batch_indices, const int32_t* positions,
                        int32_t rotary_dim, int32_t interleave, float rope_scale, float rope_theta,
                        const pa_kv_cache* cache, const int32_t* kv_indices,
-                       const int32_t* kv_indptr, int32_t batch_size, void* stream);
+                       int64_t num_kv_indices, const int32_t* kv_indptr, int32_t batch_size,
+                       void* stream);
 
 /* Diagnostic with no reference counterpart: launches one warp that waits on
  * a barrier nothing completes, with a limit of limit_cycles SM clocks (at

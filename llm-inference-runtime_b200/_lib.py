@@ -61,7 +61,7 @@ SIGNATURES = {
     "pa_append_paged_kv_cache": (
         c_int32,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int32,
-         POINTER(PagedKVCache), c_void_p, c_void_p, c_int32, c_void_p],
+         POINTER(PagedKVCache), c_void_p, c_int64, c_void_p, c_int32, c_void_p],
     ),
     "pa_apply_rope_pos_ids_inplace": (
         c_int32,
@@ -72,7 +72,7 @@ SIGNATURES = {
         c_int32,
         [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64,
          c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_float, c_float,
-         POINTER(PagedKVCache), c_void_p, c_void_p, c_int32, c_void_p],
+         POINTER(PagedKVCache), c_void_p, c_int64, c_void_p, c_int32, c_void_p],
     ),
     "pa_build_decode_tables": (
         c_int32,
@@ -94,7 +94,7 @@ SIGNATURES = {
         c_int32,
         [c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64,
          c_void_p, c_void_p, c_int32, c_int32, c_float, c_float, POINTER(PagedKVCache), c_void_p,
-         c_void_p, c_int32, c_void_p],
+         c_int64, c_void_p, c_int32, c_void_p],
     ),
     "pa_selftest_wait_timeout": (c_int32, [c_int64, c_void_p]),
     "pa_decode_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32, c_int32]),

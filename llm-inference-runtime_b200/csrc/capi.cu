@@ -294,9 +294,9 @@ int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64
                              const void* append_value, int64_t value_stride_n,
                              int64_t value_stride_h, const int32_t* batch_indices,
                              const int32_t* positions, int32_t nnz, const pa_kv_cache* cache,
-                             const int32_t* kv_indices, const int32_t* kv_indptr,
-                             int32_t batch_size, void* stream) {
-  if (nnz < 0 || batch_size < 0) return PA_ERR_INVALID_ARGUMENT;
+                             const int32_t* kv_indices, int64_t num_kv_indices,
+                             const int32_t* kv_indptr, int32_t batch_size, void* stream) {
+  if (nnz < 0 || batch_size < 0 || num_kv_indices < 0) return PA_ERR_INVALID_ARGUMENT;
   if (nnz == 0) return PA_OK;
   if (cache == nullptr || append_key == nullptr || append_value == nullptr ||
       batch_indices == nullptr || positions == nullptr || kv_indices == nullptr ||
@@ -330,6 +330,7 @@ int pa_append_paged_kv_cache(const void* append_key, int64_t key_stride_n, int64
   p.token_stride = cache->token_stride * 2;
   p.num_pages = cache->num_pages;
   p.kv_indices = kv_indices;
+  p.num_kv_indices = num_kv_indices;
   p.kv_indptr = kv_indptr;
   p.batch = batch_size;
   p.num_kv_heads = cache->num_kv_heads;
@@ -383,8 +384,10 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
                          const int32_t* positions, int32_t nnz, int32_t num_qo_heads,
                          int32_t rotary_dim, int32_t interleave, float rope_scale,
                          float rope_theta, const pa_kv_cache* cache, const int32_t* kv_indices,
-                         const int32_t* kv_indptr, int32_t batch_size, void* stream) {
-  if (nnz < 0 || batch_size < 0 || num_qo_heads < 0) return PA_ERR_INVALID_ARGUMENT;
+                         int64_t num_kv_indices, const int32_t* kv_indptr, int32_t batch_size,
+                         void* stream) {
+  if (nnz < 0 || batch_size < 0 || num_qo_heads < 0 || num_kv_indices < 0)
+    return PA_ERR_INVALID_ARGUMENT;
   if (nnz == 0) return PA_OK;
   if (cache == nullptr || q == nullptr || k == nullptr || v == nullptr ||
       batch_indices == nullptr || positions == nullptr || kv_indices == nullptr ||
@@ -409,8 +412,8 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
                                                  cache->dtype, stream);
     if (rc != PA_OK) return rc;
     return pa_append_paged_kv_cache(k, k_stride_n, k_stride_h, v, v_stride_n, v_stride_h,
-                                    batch_indices, positions, nnz, cache, kv_indices, kv_indptr,
-                                    batch_size, stream);
+                                    batch_indices, positions, nnz, cache, kv_indices,
+                                    num_kv_indices, kv_indptr, batch_size, stream);
   }
   RopeAppendParams p;
   p.q = static_cast<uint8_t*>(q);
@@ -439,6 +442,7 @@ int pa_apply_rope_append(void* q, int64_t q_stride_n, int64_t q_stride_h, void* 
   p.token_stride = cache->token_stride * 2;
   p.num_pages = cache->num_pages;
   p.kv_indices = kv_indices;
+  p.num_kv_indices = num_kv_indices;
   p.kv_indptr = kv_indptr;
   p.batch = batch_size;
   p.page_size = cache->page_size;
@@ -569,8 +573,10 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
                        int64_t q_stride_n, const int32_t* batch_indices, const int32_t* positions,
                        int32_t rotary_dim, int32_t interleave, float rope_scale, float rope_theta,
                        const pa_kv_cache* cache, const int32_t* kv_indices,
-                       const int32_t* kv_indptr, int32_t batch_size, void* stream) {
-  if (num_tokens < 0 || hidden <= 0 || num_qo_heads <= 0 || batch_size < 0)
+                       int64_t num_kv_indices, const int32_t* kv_indptr, int32_t batch_size,
+                       void* stream) {
+  if (num_tokens < 0 || hidden <= 0 || num_qo_heads <= 0 || batch_size < 0 ||
+      num_kv_indices < 0)
     return PA_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return PA_OK;
   if (x == nullptr || weight == nullptr || q_out == nullptr || cache == nullptr ||
@@ -617,6 +623,7 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
   p.token_stride = cache->token_stride * 2;
   p.num_pages = cache->num_pages;
   p.kv_indices = kv_indices;
+  p.num_kv_indices = num_kv_indices;
   p.kv_indptr = kv_indptr;
   p.batch = batch_size;
   p.page_size = cache->page_size;

@@ -47,6 +47,7 @@ struct AppendParams {
   int64_t page_stride, head_stride, token_stride;  // bytes
   int64_t num_pages;
   const int32_t* kv_indices;
+  int64_t num_kv_indices;  // entries kv_indptr may index
   const int32_t* kv_indptr;
   int batch;
   int num_kv_heads, page_size, row_chunks;  // row_chunks = head_dim * elem / 16
@@ -77,7 +78,7 @@ __global__ void append_kernel(const AppendParams p) {
     }
     const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
     const int pi = start + pos / p.page_size;
-    if (pi >= end) {
+    if (start < 0 || end > p.num_kv_indices || pi >= end) {
       set_status(PA_ERR_DEVICE_CHECK);
       continue;
     }
@@ -162,6 +163,7 @@ struct RopeAppendParams {
   int64_t page_stride, head_stride, token_stride;  // bytes
   int64_t num_pages;
   const int32_t* kv_indices;
+  int64_t num_kv_indices;  // entries kv_indptr may index
   const int32_t* kv_indptr;
   int batch, page_size;
 };
@@ -178,7 +180,7 @@ __device__ __forceinline__ int64_t rope_append_slot(const RopeAppendParams& p, i
   }
   const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
   const int pi = start + pos / p.page_size;
-  if (pi >= end) {
+  if (start < 0 || end > p.num_kv_indices || pi >= end) {
     set_status(PA_ERR_DEVICE_CHECK);
     return -1;
   }

@@ -51,6 +51,7 @@ struct QkvParams {
   int64_t page_stride, head_stride, token_stride;  // bytes
   int64_t num_pages;
   const int32_t* kv_indices;
+  int64_t num_kv_indices;  // entries kv_indptr may index
   const int32_t* kv_indptr;
   int batch, page_size;
 };
@@ -66,7 +67,7 @@ __device__ __forceinline__ int64_t qkv_slot(const QkvParams& p, int m, int h) {
   }
   const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
   const int pi = start + pos / p.page_size;
-  if (pi >= end) {
+  if (start < 0 || end > p.num_kv_indices || pi >= end) {
     set_status(PA_ERR_DEVICE_CHECK);
     return -1;
   }

@@ -174,8 +174,8 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor,
     kv_indptr = _i32_on(kv_indptr, device, "kv_indptr")
     _lib.check(_lib.load().pa_append_paged_kv_cache(
         _p(append_key), ksn, ksh, _p(append_value), vsn, vsh, _p(batch_indices), _p(positions),
-        nnz, ctypes.byref(desc), _p(kv_indices), _p(kv_indptr), kv_indptr.numel() - 1,
-        _stream()), "append_paged_kv_cache")
+        nnz, ctypes.byref(desc), _p(kv_indices), kv_indices.numel(), _p(kv_indptr),
+        kv_indptr.numel() - 1, _stream()), "append_paged_kv_cache")
     _after("append_paged_kv_cache")
 
 
@@ -230,8 +230,8 @@ def apply_rope_append(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     _lib.check(_lib.load().pa_apply_rope_append(
         _p(q), qsn, qsh, _p(k), ksn, ksh, _p(v), vsn, vsh, _p(batch_indices), _p(positions),
         q.size(0), q.size(1), rotary_dim, int(bool(interleave)), float(rope_scale),
-        float(rope_theta), ctypes.byref(desc), _p(kv_indices), _p(kv_indptr),
-        kv_indptr.numel() - 1, _stream()), "apply_rope_append")
+        float(rope_theta), ctypes.byref(desc), _p(kv_indices), kv_indices.numel(),
+        _p(kv_indptr), kv_indptr.numel() - 1, _stream()), "apply_rope_append")
     _after("apply_rope_append")
 
 

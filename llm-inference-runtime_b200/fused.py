@@ -63,7 +63,7 @@ def qkv_rope_append(x: torch.Tensor, weight: torch.Tensor, num_qo_heads: int,
         x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), m, x.size(1),
         num_qo_heads, q_out.data_ptr(), q_out.stride(0), batch_indices.data_ptr(),
         positions.data_ptr(), rotary_dim, int(bool(interleave)), float(rope_scale),
-        float(rope_theta), ctypes.byref(desc), kv_indices.data_ptr(), kv_indptr.data_ptr(),
-        kv_indptr.numel() - 1, _stream()), "qkv_rope_append")
+        float(rope_theta), ctypes.byref(desc), kv_indices.data_ptr(), kv_indices.numel(),
+        kv_indptr.data_ptr(), kv_indptr.numel() - 1, _stream()), "qkv_rope_append")
     _after("qkv_rope_append")
     return q_out

@@ -228,3 +228,35 @@ def test_rope_append_flags_out_of_range_position(fi, lir):
     finally:
         fa._CHECK = saved
     assert torch.count_nonzero(pool) == 0
+
+
+@pytest.mark.parametrize("op", ["append", "rope_append"])
+def test_append_flags_indptr_past_the_page_ids(fi, lir, op):
+    """kv_indptr ranges must lie inside kv_indices: request 1 claims pages
+    2..8 of a 3-entry index array, and a negative start is as bad. Those rows
+    are skipped with a device check (no page id is read from outside the
+    array); request 0's row lands in its page."""
+    import importlib
+    fa = importlib.import_module("llm-inference-runtime_b200.flashinfer_api")
+    for indptr in ([0, 2, 9], [-1, 2, 3]):
+        pool = torch.zeros(4, 2, 4, 16, 64, dtype=torch.bfloat16, device=DEV)
+        q = torch.ones(2, 32, 64, dtype=torch.bfloat16, device=DEV)
+        k = torch.ones(2, 4, 64, dtype=torch.bfloat16, device=DEV)
+        torch.cuda.synchronize()
+        lir._lib.device_status()
+        saved = fa._CHECK
+        fa._CHECK = False
+        try:
+            args = (_t([0, 1]), _t([3, 20]), pool, _t([1, 2, 3]), _t(indptr), _t([5, 5]))
+            if op == "append":
+                fi.append_paged_kv_cache(k, k, *args, kv_layout="HND")
+            else:
+                fi.apply_rope_append(q, k, k.clone(), *args, kv_layout="HND")
+            assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
+        finally:
+            fa._CHECK = saved
+        written = torch.nonzero(pool.abs().sum(dim=(1, 2, 4))).tolist()
+        if indptr[0] == 0:  # request 0 is valid: its row goes to page 1, slot 3
+            assert written == [[1, 3]]
+        else:
+            assert written == []
