@@ -69,7 +69,14 @@ typedef struct pa_kv_cache {
 /* Human-readable name of a status code (static string). */
 const char* pa_status_string(int status);
 
-/* ABI version of this library (major * 100 + minor). */
+/* ABI version this header describes (major * 100 + minor). 101: the append,
+ * RoPE + append, fused QKV and cascade-plan calls take the number of page ids
+ * (num_kv_indices) after kv_indptr. A caller built against another version
+ * must refuse the library (the Python binding does). */
+#define PA_ABI_VERSION 101
+
+/* ABI version of this library (major * 100 + minor); equals PA_ABI_VERSION
+ * of the header it was built from. */
 int pa_abi_version(void);
 
 /* Reads and clears the device-side status word of the current device.

@@ -31,6 +31,10 @@ PA_DTYPE_BF16 = 1
 
 PA_NOALLOC_SCRATCH_BYTES = 24 * 1024 * 1024
 
+# PA_ABI_VERSION of include/paged_attn.h that SIGNATURES mirrors; a library
+# reporting another version is refused (argument lists would not line up).
+ABI_VERSION = 101
+
 
 class PagedKVCache(ctypes.Structure):
     """Mirror of ``pa_kv_cache``."""
@@ -172,6 +176,11 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+        got = lib.pa_abi_version()
+        if got != ABI_VERSION:
+            raise RuntimeError(
+                f"{LIB_NAME} reports ABI version {got}, this binding needs {ABI_VERSION}; "
+                "rebuild the library from this checkout")
         _lib = lib
     return _lib
 

@@ -267,7 +267,7 @@ const char* pa_status_string(int status) {
   }
 }
 
-int pa_abi_version(void) { return 100; }
+int pa_abi_version(void) { return PA_ABI_VERSION; }
 
 int pa_device_status(void) {
   if (cudaDeviceSynchronize() != cudaSuccess) return PA_ERR_CUDA;
@@ -957,12 +957,6 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
 
 namespace {
 
-// Level-0 work items aim at (SMs / PA_CASCADE_SM_SHARE) CTAs (tunable at
-// build time).
-#ifndef PA_CASCADE_SM_SHARE
-#define PA_CASCADE_SM_SHARE 1
-#endif
-
 // Cascade geometry for a batch: level-0 chunk count sized so the chunks'
 // prefill items fill the SMs once, the decode partition of level 1, and the
 // workspace layout of both.
@@ -980,7 +974,9 @@ bool cascade_shape(int dev, int batch, int hq, int hkv, int head_dim, CascadeSha
   s->span = 2 * s->qt;
   const int nq = (batch + s->span - 1) / s->span;
   const int per_chunk = hkv * nq;
-  const int target = std::max(1, s->dec.ctas / PA_CASCADE_SM_SHARE);
+  // level-0 items fill the SMs once (fewer, longer chunks lengthen each
+  // CTA's chain more than they shorten the merge)
+  const int target = std::max(1, s->dec.ctas);
   s->max_chunks = std::max(1, std::min((target + per_chunk - 1) / per_chunk, kCascadeMaxChunks));
   s->L = cascade_ws_layout(batch, hq, hkv, head_dim, s->max_chunks, s->span, s->dec.units,
                            s->dec.g.hb);

@@ -77,7 +77,7 @@ __global__ void append_kernel(const AppendParams p) {
       continue;
     }
     const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
-    const int pi = start + pos / p.page_size;
+    const int64_t pi = static_cast<int64_t>(start) + pos / p.page_size;
     if (start < 0 || end > p.num_kv_indices || pi >= end) {
       set_status(PA_ERR_DEVICE_CHECK);
       continue;
@@ -179,7 +179,7 @@ __device__ __forceinline__ int64_t rope_append_slot(const RopeAppendParams& p, i
     return -1;
   }
   const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
-  const int pi = start + pos / p.page_size;
+  const int64_t pi = static_cast<int64_t>(start) + pos / p.page_size;
   if (start < 0 || end > p.num_kv_indices || pi >= end) {
     set_status(PA_ERR_DEVICE_CHECK);
     return -1;

@@ -34,28 +34,6 @@
 
 namespace pa {
 
-// Share of the softmax exponentials evaluated on the FMA pipe instead of the
-// MUFU unit (column c uses the polynomial when c % 8 < kPfPolyOf8).
-#ifndef PA_PF_POLY_OF8
-#define PA_PF_POLY_OF8 0
-#endif
-constexpr int kPfPolyOf8 = PA_PF_POLY_OF8;
-
-// 2^x evaluated with FMA / integer instructions: x = n + f, n = round(x),
-// f in [-0.5, 0.5]; 2^f from a cubic fitted to 2^f on that interval
-// (weighted least squares, max relative error 7.5e-5), then n is added to
-// the exponent field. x below -126 (including -inf) returns 0.
-__device__ __forceinline__ float exp2_fma(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float t = xc + 12582912.0f;  // 1.5 * 2^23: the low mantissa bits hold round(xc)
-  const float n = t - 12582912.0f;
-  const float f = xc - n;
-  const float p = fmaf(fmaf(fmaf(0.05517605f, f, 0.24261150f), f, 0.69326019f), f, 0.99992806f);
-  const int ni = __float_as_int(t) - 0x4B400000;
-  const float r = __int_as_float(__float_as_int(p) + (ni << 23));
-  return x < -126.0f ? 0.0f : r;
-}
-
 // Two non-negative fp32 values -> packed 16-bit pair (lo in the low half).
 // Both types: the hardware round-to-nearest-even conversion, one instruction
 // per pair.
@@ -93,14 +71,8 @@ constexpr int kPfBarV = 4;
 constexpr int kPfBarPThreads = 128 + 32;
 constexpr int kPfBarKVThreads = 32 + 32;
 constexpr int kPfThreads = 384;
-#ifndef PA_PF_REGS_SOFTMAX
-#define PA_PF_REGS_SOFTMAX 224
-#endif
-#ifndef PA_PF_REGS_OTHER
-#define PA_PF_REGS_OTHER 56
-#endif
-constexpr uint32_t kPfRegsSoftmax = PA_PF_REGS_SOFTMAX;
-constexpr uint32_t kPfRegsOther = PA_PF_REGS_OTHER;
+constexpr uint32_t kPfRegsSoftmax = 224;
+constexpr uint32_t kPfRegsOther = 56;
 static_assert(2 * 128 * kPfRegsSoftmax + 128 * kPfRegsOther <= kPfThreads * 168,
               "register split must fit the launch allocation");
 static_assert(kPfRegsSoftmax % 8 == 0 && kPfRegsOther % 8 == 0 && kPfRegsOther >= 24,
@@ -533,7 +505,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
         for (int c = 32 * ch; c < 32 * ch + 32; ++c) {
           const float x = fmaf(s[c], p.scale_log2, neg_m);
-          s[c] = (c & 7) < kPfPolyOf8 ? exp2_fma(x) : ex2(x);
+          s[c] = ex2(x);
           l4[c & 3] += s[c];
         }
 #pragma unroll

@@ -66,7 +66,7 @@ __device__ __forceinline__ int64_t qkv_slot(const QkvParams& p, int m, int h) {
     return -1;
   }
   const int start = __ldg(p.kv_indptr + b), end = __ldg(p.kv_indptr + b + 1);
-  const int pi = start + pos / p.page_size;
+  const int64_t pi = static_cast<int64_t>(start) + pos / p.page_size;
   if (start < 0 || end > p.num_kv_indices || pi >= end) {
     set_status(PA_ERR_DEVICE_CHECK);
     return -1;

@@ -35,7 +35,39 @@ from . import fused
 _FUSED_QKV = os.environ.get("PA_FUSED_QKV", "0") == "1"
 
 
-class PagedAttnState:
+class _StateMeta(type):
+    """Class-level ``batch_indices`` / ``positions`` whose build can wait.
+
+    ``build_batch_indices_positions`` called without ``nnz`` (the engine's
+    own call, step_executor.py:155) records its inputs instead of reading
+    ``nnz`` back from the device; the first patched layer of the step builds
+    the tensors with ``nnz`` = its number of q rows. Assigning either
+    attribute directly (the engine's decode path, step_executor.py:216-221)
+    drops a pending build. Reading one while a build is pending builds it
+    with ``nnz`` read from the device, the reference's behaviour.
+    """
+
+    def _get_batch_indices(cls):
+        cls._resolve_pending(None)
+        return cls._batch_indices
+
+    def _set_batch_indices(cls, value):
+        cls._pending = None
+        cls._batch_indices = value
+
+    def _get_positions(cls):
+        cls._resolve_pending(None)
+        return cls._positions
+
+    def _set_positions(cls, value):
+        cls._pending = None
+        cls._positions = value
+
+    batch_indices = property(_get_batch_indices, _set_batch_indices)
+    positions = property(_get_positions, _set_positions)
+
+
+class PagedAttnState(metaclass=_StateMeta):
     """Per-process attention state (the reference's FlashInferState)."""
 
     kv_pool: Optional[torch.Tensor] = None
@@ -44,8 +76,21 @@ class PagedAttnState:
     kv_indptr: Optional[torch.Tensor] = None
     kv_last_page_len: Optional[torch.Tensor] = None
 
-    batch_indices: Optional[torch.Tensor] = None
-    positions: Optional[torch.Tensor] = None
+    # batch_indices / positions: properties of the metaclass (above)
+    _batch_indices: Optional[torch.Tensor] = None
+    _positions: Optional[torch.Tensor] = None
+    _pending: Optional[tuple] = None  # (append_indptr, seq_lens) awaiting nnz
+
+    @classmethod
+    def _resolve_pending(cls, nnz: Optional[int]) -> None:
+        if cls._pending is None:
+            return
+        append_indptr, seq_lens = cls._pending
+        if nnz is None:
+            nnz = int(append_indptr[-1].item())
+        cls._pending = None
+        cls._batch_indices, cls._positions = flashinfer.get_batch_indices_positions(
+            append_indptr, seq_lens, nnz)
 
     workspace_buffer: Optional[torch.Tensor] = None
 
@@ -84,11 +129,15 @@ def build_batch_indices_positions(append_indptr: torch.Tensor, seq_lens: torch.T
     """Sets the per-row request ids and positions for RoPE and the KV append.
 
     The reference reads ``nnz`` back from the device (``.item()``,
-    llama.py:74). Callers that know it (it is the length of the step's
-    input ids) pass it and the call never synchronises.
+    llama.py:74), which synchronises the host with the GPU every prefill
+    step. Here, without ``nnz``, the build waits for the step's first
+    patched layer, whose q rows number ``nnz`` (the step's input ids), so
+    the call never synchronises and can be captured in a CUDA graph.
+    Callers that know ``nnz`` may pass it; the build then runs at once.
     """
     if nnz is None:
-        nnz = int(append_indptr[-1].item())
+        PagedAttnState._pending = (append_indptr, seq_lens)
+        return
     (PagedAttnState.batch_indices,
      PagedAttnState.positions) = flashinfer.get_batch_indices_positions(
         append_indptr, seq_lens, nnz)
@@ -126,6 +175,7 @@ def paged_attention(attn, q_flat: torch.Tensor, k_flat: torch.Tensor,
     The body of the reference's patched forward between the QKV and output
     projections (llama.py:173-245). Returns [rows, H_q, D].
     """
+    PagedAttnState._resolve_pending(q_flat.shape[0])
     positions = cast(torch.Tensor, PagedAttnState.positions)
     kv_pool = cast(torch.Tensor, PagedAttnState.kv_pool)
     layer_kv_cache = kv_pool[attn.layer_idx]
@@ -151,6 +201,7 @@ def paged_attention_fused(attn, x: torch.Tensor, weight: torch.Tensor) -> torch.
     """As paged_attention, starting from the layer input: the fused QKV
     projection kernel produces the rotated q and appends k / v, then the
     prefill or decode attention runs. Returns [rows, H_q, D]."""
+    PagedAttnState._resolve_pending(x.shape[0])
     kv_pool = cast(torch.Tensor, PagedAttnState.kv_pool)
     layer_kv_cache = kv_pool[attn.layer_idx]
     q_flat = fused.qkv_rope_append(

@@ -37,7 +37,22 @@ def test_status_strings(lir):
     lir.build.build()
     assert lir._lib.status_string(0) == "ok"
     assert "unsupported" in lir._lib.status_string(lir._lib.PA_ERR_UNSUPPORTED)
-    assert lir._lib.load().pa_abi_version() == 100
+    assert lir._lib.load().pa_abi_version() == lir._lib.ABI_VERSION
+
+
+def test_header_and_binding_name_the_same_abi_version(lir):
+    import re
+    with open(os.path.join(REPO, "include", "paged_attn.h")) as f:
+        m = re.search(r"#define PA_ABI_VERSION (\d+)", f.read())
+    assert m and int(m.group(1)) == lir._lib.ABI_VERSION
+
+
+def test_library_of_another_abi_version_is_refused(lir, monkeypatch):
+    lir.build.build()
+    monkeypatch.setattr(lir._lib, "_lib", None)
+    monkeypatch.setattr(lir._lib, "ABI_VERSION", lir._lib.ABI_VERSION + 1)
+    with pytest.raises(RuntimeError, match="ABI version"):
+        lir._lib.load()
 
 
 def test_host_side_validation_without_launch(lir):

@@ -230,7 +230,7 @@ def test_rope_append_flags_out_of_range_position(fi, lir):
     assert torch.count_nonzero(pool) == 0
 
 
-@pytest.mark.parametrize("op", ["append", "rope_append"])
+@pytest.mark.parametrize("op", ["append", "rope_append", "qkv_rope_append"])
 def test_append_flags_indptr_past_the_page_ids(fi, lir, op):
     """kv_indptr ranges must lie inside kv_indices: request 1 claims pages
     2..8 of a 3-entry index array, and a negative start is as bad. Those rows
@@ -250,8 +250,15 @@ def test_append_flags_indptr_past_the_page_ids(fi, lir, op):
             args = (_t([0, 1]), _t([3, 20]), pool, _t([1, 2, 3]), _t(indptr), _t([5, 5]))
             if op == "append":
                 fi.append_paged_kv_cache(k, k, *args, kv_layout="HND")
-            else:
+            elif op == "rope_append":
                 fi.apply_rope_append(q, k, k.clone(), *args, kv_layout="HND")
+            else:  # the fused QKV projection's epilogue takes the same page-table checks
+                fused = importlib.import_module("llm-inference-runtime_b200.fused")
+                x = torch.full((2, 2048), 0.01, dtype=torch.bfloat16, device=DEV)
+                w = torch.full(((32 + 2 * 4) * 64, 2048), 0.01, dtype=torch.bfloat16,
+                               device=DEV)
+                fused.qkv_rope_append(x, w, 32, args[0], args[1], pool, args[3], args[4],
+                                      kv_layout="HND")
             assert lir._lib.device_status() == lir._lib.PA_ERR_DEVICE_CHECK
         finally:
             fa._CHECK = saved
