@@ -1,19 +1,19 @@
-"""Benchmark of the paged-decode attention path (one JSON line on rank 0).
+"""Benchmark of the paged-attention path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg1|cfg2|cfg3|cfg4|cfg5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|flashinfer]
+                    [--workload cfg1|cfg2|cfg3|cfg4|cfg5] [--headline-only]
 
 Metric: paged-decode attention HBM GB/s (fraction of the
 measured HBM peak) and decode tok/s, at 1/2/4/8 B200.
 
-Workload (default cfg2 = configuration 2): the attention of a TinyLlama-1.1B
-decode step — 22 layers, 32 q / 4 kv heads, head_dim 64, bf16 — for 256
-requests per GPU with contexts ~ U[1024, 4096], page size 16, KV pre-filled
-N(0,1), page ids a random permutation of the pool. One step = the device
-plan + batch indices/positions once, then for each of the 22 layers the KV
-append of the step's token and the decode attention — one launch per layer
-(run_with_append; FlashInfer's arm makes the reference's two calls,
-append_paged_kv_cache then run). Requests are sharded
+Headline workload (default cfg2 = configuration 2): the attention of a
+TinyLlama-1.1B decode step — 22 layers, 32 q / 4 kv heads, head_dim 64,
+bf16 — for 256 requests per GPU with contexts ~ U[1024, 4096], page size 16,
+KV pre-filled N(0,1), page ids a random permutation of the pool. One step =
+the device plan + batch indices/positions once, then for each of the 22
+layers the KV append of the step's token and the decode attention — one
+launch per layer (run_with_append; FlashInfer's arm makes the reference's
+two calls, append_paged_kv_cache then run). Requests are sharded
 round-robin over GPUs (weak scaling: 256 per GPU), each GPU owning its pool;
 no data-path collective (gloo is used only for the barrier and the max over
 ranks of the timed region).
@@ -21,13 +21,22 @@ ranks of the timed region).
 value = algorithmic bytes of all ranks (every K/V element read once, q read,
 o written, appended rows read + written) / max-over-ranks device time of
 the step replayed from a CUDA graph (captured once after warm-up; --eager
-times eager launches instead). The same steps are also timed with eager
-launches first: the per-launch events of that loop give the decode kernel's
-duration for the roofline, and its step time is reported as
-eager_ms_per_step.
+times eager launches instead). roofline.avg_launch_ms is one event span
+around the 22 decode launches inside that same replayed graph, divided by
+22. The same steps are also timed with eager launches (eager_ms_per_step).
 e2e = the same bytes / device time of the same step driven through the
 public API from pinned host buffers (tables, q, new K/V copied in; outputs
 copied out every layer).
+
+Unless --headline-only (or another --workload) is given, the same line also
+carries the other configurations, each measured the same way after the
+previous one's memory is freed: prefill_cfg3 (the mixed chunked-prefill +
+decode step, with the prefill kernel's tensor roofline), long_cfg5 (512
+requests of 8-32 k tokens, split across the GPUs: strong scaling),
+cascade_cfg4 (64 requests sharing a 2048-token prefix: plain decode and the
+two-level cascade, logical and unique bytes) and small_cfg1 (8 requests).
+With N > 1 the line adds per-rank figures (per_rank) of every rank's step
+time, decode roofline fraction, e2e throughput and host-copy rates.
 
 --impl reference: the reference's attention math on the host cores (the
 CPU oracle: fp32 eager attention over gathered pages), rank 0 only, each
@@ -151,17 +160,31 @@ class ClockSampler:
                 "power_w_max": max(power) if power else None}
 
 
-def _workload(args):
+# workload name -> (geometry name, requests per GPU (global for strong scaling),
+# context lo, hi, layers, description)
+WORKLOADS = {
+    "cfg1": ("TINYLLAMA", 8, 16, 512, 22, "cfg1 TinyLlama-1.1B decode step, 8 requests"),
+    "cfg2": ("TINYLLAMA", 256, 1024, 4096, 22, "cfg2 TinyLlama-1.1B decode step attention"),
+    "cfg3": ("LLAMA3_8B", 128, 256, 4096, 1, "cfg3 chunked-prefill mixed batch (decode part)"),
+    "cfg4": ("LLAMA3_8B", 64, 32, 256, 1, "cfg4 64 requests sharing a 2048-token prefix"),
+    "cfg5": ("LLAMA3_8B", 512, 8192, 32768, 1, "cfg5 long-context split-KV decode"),
+}
+
+
+def _workload(name: str):
     wl = importlib.import_module(PKG + ".workloads")
-    if args.workload == "cfg1":
-        return wl, wl.TINYLLAMA, 8, 16, 512, 22, "cfg1 TinyLlama-1.1B decode step, 8 requests"
-    if args.workload == "cfg4":
-        return wl, wl.LLAMA3_8B, 64, 32, 256, 1, "cfg4 64 requests sharing a 2048-token prefix"
-    if args.workload == "cfg3":
-        return wl, wl.LLAMA3_8B, 128, 256, 4096, 1, "cfg3 chunked-prefill mixed batch (decode part)"
-    if args.workload == "cfg5":
-        return wl, wl.LLAMA3_8B, 512, 8192, 32768, 1, "cfg5 long-context split-KV decode"
-    return wl, wl.TINYLLAMA, 256, 1024, 4096, 22, "cfg2 TinyLlama-1.1B decode step attention"
+    gname, per_gpu, lo, hi, layers, desc = WORKLOADS[name]
+    return wl, getattr(wl, gname), per_gpu, lo, hi, layers, desc
+
+
+def _gather(x, world: int) -> list:
+    """Every rank's value of x, in rank order (rank 0 alone: [x])."""
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, x)
+    return out
 
 
 def _global_lengths(batch_total: int, lo: int, hi: int, seed: int = 0) -> np.ndarray:
@@ -199,23 +222,28 @@ def _check(lir, ours: bool, what: str) -> None:
 
 
 # ------------------------------------------------------------------ ours
-def run_ours(args):
-    rank, world, local = _dist()
+def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float = 15.0):
+    """One decode workload (cfg1 / cfg2 / cfg4 / cfg5) on every rank; returns
+    rank 0's line (None on the other ranks). strong: the workload's request
+    count is the global batch, split round-robin over the ranks (otherwise
+    each rank serves that many requests: weak scaling)."""
+    rank, world, local = ctx
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lir = importlib.import_module(PKG)
     fi, ours = _backend(args)
-    wl, geom, per_gpu, lo, hi, layers, wname = _workload(args)
+    wl, geom, per_gpu, lo, hi, layers, wname = _workload(workload)
     P = geom.page_size
 
-    # weak scaling: global batch per_gpu * world, request i on GPU i mod world
-    if args.workload == "cfg4":
+    total_requests = per_gpu if strong else per_gpu * world
+    if workload == "cfg4":
         # every GPU serves its own 64 requests over one shared 2048-token prefix
         prob = wl.make_shared_prefix_problem(geom, per_gpu, 2048, lo, hi, seed=1000 + rank,
                                              device=dev, num_layers=layers)
     else:
-        lengths_all = _global_lengths(per_gpu * world, lo, hi)
-        mine = wl.round_robin(per_gpu * world, world, rank)
+        # request i on GPU i mod world
+        lengths_all = _global_lengths(total_requests, lo, hi)
+        mine = wl.round_robin(total_requests, world, rank)
         prob = wl.make_decode_problem(geom, len(mine), 0, 0, seed=1000 + rank, device=dev,
                                       num_layers=layers, lengths=lengths_all[mine])
     B = prob.batch
@@ -239,7 +267,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     dec_events = []
 
-    def step(record: bool):
+    def step(record: bool, span=None):
         bi, pos = fi.get_batch_indices_positions(append_indptr, seq, B)
         wrap.plan(indptr, indices, last, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim,
                   P, q_data_type=q.dtype)
@@ -248,9 +276,9 @@ def run_ours(args):
         # stop each launch from overlapping its predecessor's tail) and
         # divided by the layer count; FlashInfer's interleave append kernels,
         # so each of its decode launches is bracketed alone.
-        span = None
         if record and ours:
             span = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        if span is not None:
             span[0].record(stream)
         for layer in range(layers):
             if not ours:
@@ -269,12 +297,13 @@ def run_ours(args):
                 dec_events.append((e0, e1, 1))
         if span is not None:
             span[1].record(stream)
-            dec_events.append((span[0], span[1], layers))
+            if record:
+                dec_events.append((span[0], span[1], layers))
 
     for _ in range(args.warmup):
         step(False)
     torch.cuda.synchronize()
-    _check(lir, ours, "bench warm-up")
+    _check(lir, ours, f"bench {workload} warm-up")
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -291,7 +320,7 @@ def run_ours(args):
     small = unique_kv < (100 << 20)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if small else None
 
-    def timed(run_step) -> float:
+    def timed(run_step, after=None) -> float:
         if small:
             total = 0.0
             for _ in range(args.steps):
@@ -301,6 +330,8 @@ def run_ours(args):
                 t1.record(stream)
                 torch.cuda.synchronize()
                 total += t0.elapsed_time(t1)
+                if after is not None:
+                    after()
             return total
         t0.record(stream)
         for _ in range(args.steps):
@@ -309,33 +340,56 @@ def run_ours(args):
         torch.cuda.synchronize()
         return t0.elapsed_time(t1)
 
-    # Eager launches (the per-launch events give the decode kernel's duration
-    # for the roofline), then -- this package only -- the same step captured
-    # once in a CUDA graph and replayed, which is how a serving loop runs a
-    # launch-bound decode step. FlashInfer's plan works on the host and cannot
-    # be captured, so its arm stays eager.
+    # Eager launches first, then -- this package only -- the same step
+    # captured once in a CUDA graph and replayed, which is how a serving loop
+    # runs a launch-bound decode step. The graph holds one event pair around
+    # its decode launches (record nodes of external events): after the timed
+    # replays, the same graph is replayed once per step with a read of that
+    # span, which gives the decode kernel's duration for the roofline inside
+    # the step that value times. FlashInfer's plan works on the host and
+    # cannot be captured, so its arm stays eager and its decode launches are
+    # timed one by one.
     eager_local = timed(lambda: step(True))
     graph = None
+    spans = []
     if ours and not args.eager:
+        gspan = (torch.cuda.Event(enable_timing=True, external=True),
+                 torch.cuda.Event(enable_timing=True, external=True))
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            step(False)
+            step(False, span=gspan)
         graph.replay()
         torch.cuda.synchronize()
         _barrier(world)
         ms_local = timed(graph.replay)
+        _barrier(world)
+        if small:
+            timed(graph.replay, after=lambda: spans.append(gspan[0].elapsed_time(gspan[1])))
+        else:
+            for _ in range(args.steps):
+                graph.replay()
+                torch.cuda.synchronize()
+                spans.append(gspan[0].elapsed_time(gspan[1]))
     else:
         ms_local = eager_local
     _barrier(world)
     clocks = sampler.stop()
     ms = _max_over_ranks(ms_local, world)
     eager_ms = _max_over_ranks(eager_local, world)
-    dec_ms = (sum(a.elapsed_time(b) for a, b, _ in dec_events)
-              / sum(n for _, _, n in dec_events))
+    if spans:
+        dec_ms_local = statistics.mean(spans) / layers
+        dec_timing = "one event span around the decode launches inside the replayed step graph"
+    else:
+        dec_ms_local = (sum(a.elapsed_time(b) for a, b, _ in dec_events)
+                        / sum(n for _, _, n in dec_events))
+        dec_timing = "event pairs around each eager decode launch"
+    dec_ms = _max_over_ranks(dec_ms_local, world)
     total_bytes = _sum_over_ranks(float(bytes_step) * args.steps, world)
     value = total_bytes / (ms * 1e-3) / 1e9
     tok_s = _sum_over_ranks(float(B) * args.steps, world) / (ms * 1e-3)
-    _check(lir, ours, "bench timed region")
+    _check(lir, ours, f"bench {workload} timed region")
+    if graph is not None:
+        del graph
 
     # ---- end to end through the public API from pinned host memory
     # Every step copies its inputs in (tables once, then each layer's q and new
@@ -424,20 +478,49 @@ def run_ours(args):
         e2e_step()
     t1.record(stream)
     torch.cuda.synchronize()
+    e2e_local = t0.elapsed_time(t1)
     _barrier(world)
-    e2e_ms = _max_over_ranks(t0.elapsed_time(t1), world)
+    e2e_ms = _max_over_ranks(e2e_local, world)
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
     ok = torch.equal(h_out[layers - 1], out.cpu())  # same q, same pool state: same result
-    _check(lir, ours, "bench e2e")
+    _check(lir, ours, f"bench {workload} e2e")
+
+    # ---- host-copy rates alone: every rank moves one step's input and output
+    # bytes at the same time (the contention the e2e steps run under)
+    def copy_rate(direction: str) -> float:
+        _barrier(world)
+        torch.cuda.synchronize()
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s_in):
+            c0.record(s_in)
+            for _ in range(args.steps):
+                for layer in range(layers):
+                    b = layer % 2
+                    if direction == "h2d":
+                        d_q[b].copy_(h_q[layer], non_blocking=True)
+                        d_k[b].copy_(h_k[layer], non_blocking=True)
+                        d_v[b].copy_(h_v[layer], non_blocking=True)
+                    else:
+                        h_out[layer].copy_(d_out[b], non_blocking=True)
+            c1.record(s_in)
+        torch.cuda.synchronize()
+        n = layers * ((q.numel() + k_new.numel() + v_new.numel()) * 2 if direction == "h2d"
+                      else q.numel() * 2)
+        return n * args.steps / (c0.elapsed_time(c1) * 1e-3) / 1e9
+
+    h2d_gbs, d2h_gbs = copy_rate("h2d"), copy_rate("d2h")
+    _barrier(world)
+
     # configuration 2 is a full decode step: also time the whole model
     model = (model_step(args, ours, prob, indptr, indices, last, seq, world)
-             if args.workload == "cfg2" and not args.no_model else None)
+             if workload == "cfg2" and not args.no_model else None)
     if ours:
         _check(lir, ours, "bench model step")
     # configuration 4: the same step with the shared prefix attended once
     cascade = (cascade_step(args, fi, prob, geom, layers, seq, append_indptr, out, small, flush,
                             world, bytes_step)
-               if args.workload == "cfg4" and ours else None)
+               if workload == "cfg4" and ours else None)
     if ours:
         _check(lir, ours, "bench cascade step")
 
@@ -445,62 +528,81 @@ def run_ours(args):
     # the timed launch: decode + the step's fused append (ours), decode alone (FlashInfer)
     bytes_launch = bytes_decode + (bytes_append if ours else 0)
     achieved = bytes_launch / (dec_ms * 1e-3) / 1e9
+    per_rank = _gather({"ms_per_step": round(ms_local / args.steps, 4),
+                        "decode_frac_of_hbm": round(bytes_launch / (dec_ms_local * 1e-3) / 1e9
+                                                    / peak, 4),
+                        "e2e_gbs": round(bytes_step * args.steps / (e2e_local * 1e-3) / 1e9, 1),
+                        "h2d_gbs": round(h2d_gbs, 2), "d2h_gbs": round(d2h_gbs, 2),
+                        "requests": B}, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and ours:
-        cpu = cpu_baseline(prob_lengths=prob.lengths, geom=geom, layers=layers)
+        cpu = cpu_baseline(prob_lengths=prob.lengths, geom=geom, layers=layers,
+                           budget_s=cpu_budget_s)
     _barrier(world)
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: seeded N(0,1) q/K/V, random page permutation, random-init",
-            "step_launch": "CUDA graph replay" if graph is not None else "eager",
-            "eager_ms_per_step": round(eager_ms / args.steps, 4),
-            "config": {"workload": wname, "layers": layers,
-                       "num_qo_heads": geom.num_qo_heads, "num_kv_heads": geom.num_kv_heads,
-                       "head_dim": geom.head_dim, "page_size": P,
-                       "requests_per_gpu": B, "global_batch": per_gpu * world,
-                       "context": f"U[{lo},{hi}] + 1 appended",
-                       "parallelism": f"request-sharded x{world}, no collective",
-                       "l2": ("L2 flushed between timed steps (256 MiB read); distinct KV "
-                              f"of one layer {unique_kv / 1e6:.1f} MB" if small else
-                              "inputs larger than L2 (KV of one layer "
-                              f"{bytes_decode / 1e6:.0f} MB vs 126 MB L2)")},
-            "decode_tok_s": round(tok_s, 1),
-            **({"unique_kv_bytes_per_layer": int(prob.extra["unique_pages"]) *
-                geom.page_size * geom.kv_bytes_per_token,
-                "logical_kv_bytes_per_layer": int(prob.lengths.sum()) * geom.kv_bytes_per_token,
-                "note": "logical bytes count the shared prefix once per request; its pages "
-                        "stay in L2, so logical GB/s can exceed the HBM peak"}
-               if "unique_pages" in prob.extra else {}),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind,
-                         "kernel": "decode_kernel (step's KV append fused)" if ours
-                         else "decode_kernel",
-                         "bytes_per_launch": bytes_launch,
-                         "avg_launch_ms": round(dec_ms, 5),
-                         "traffic": _traffic_from_profile(bytes_launch) if ours else None},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
-                    "copies": "pinned host buffers, two copy streams overlapped with compute",
-                    "last_layer_matches_device_run": ok},
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-        }
-        if model is not None:
-            line["model_step"] = model
-        if cascade is not None:
-            line["cascade"] = cascade
-        if not ours:
-            _mark_flashinfer(line)
-        print(json.dumps(line), flush=True)
+    del prob, pool, ws, flush
+    if rank != 0:
+        return None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) q/K/V, random page permutation, random-init",
+        "step_launch": "CUDA graph replay" if ours and not args.eager else "eager",
+        "eager_ms_per_step": round(eager_ms / args.steps, 4),
+        "config": _config(workload, geom, layers, total_requests, world, lo, hi,
+                          "L2 flushed between timed steps (256 MiB read); distinct KV "
+                          f"of one layer {unique_kv / 1e6:.1f} MB" if small else
+                          "inputs larger than L2 (KV of one layer "
+                          f"{bytes_decode / 1e6:.0f} MB vs 126 MB L2)", strong),
+        "decode_tok_s": round(tok_s, 1),
+        **({"unique_kv_bytes_per_layer": int(unique_kv),
+            "logical_kv_bytes_per_layer": int(bytes_decode),
+            "unique_value": round(_sum_over_ranks(float(layers * unique_kv) * args.steps, world)
+                                  / (ms * 1e-3) / 1e9, 2),
+            "note": "value counts the shared prefix once per request (logical bytes); its "
+                    "pages stay in L2, so logical GB/s can exceed the HBM peak; unique_value "
+                    "counts every distinct page once"}
+           if workload == "cfg4" else {}),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_kind": peak_kind,
+                     "kernel": "decode_kernel (step's KV append fused)" if ours
+                     else "decode_kernel",
+                     "bytes_per_launch": bytes_launch,
+                     "avg_launch_ms": round(dec_ms, 5),
+                     "launch_timing": dec_timing,
+                     "traffic": _traffic_from_profile(bytes_launch, geom.head_dim) if ours
+                     else None},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
+                "copies": "pinned host buffers, two copy streams overlapped with compute",
+                "last_layer_matches_device_run": ok},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
     if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+        line["per_rank"] = per_rank
+    if model is not None:
+        line["model_step"] = model
+    if cascade is not None:
+        line["cascade"] = cascade
+    if not ours:
+        _mark_flashinfer(line)
+    return line
+
+
+def _config(workload, geom, layers, total_requests, world, lo, hi, l2, strong=False) -> dict:
+    """The config object every arm reports for a workload (same keys and
+    values on this package's, FlashInfer's and the reference's lines)."""
+    per_gpu = -(-total_requests // world) if strong else total_requests // world
+    return {"workload": WORKLOADS[workload][5], "layers": layers,
+            "num_qo_heads": geom.num_qo_heads, "num_kv_heads": geom.num_kv_heads,
+            "head_dim": geom.head_dim, "page_size": geom.page_size,
+            "requests_per_gpu": per_gpu, "global_batch": total_requests,
+            "context": f"U[{lo},{hi}] + 1 appended",
+            "parallelism": f"request-sharded x{world}, no collective", "l2": l2}
 
 
 def cascade_step(args, fi, prob, geom, layers, seq, append_indptr, plain_out, small, flush,
@@ -679,32 +781,36 @@ def model_step(args, ours: bool, prob, indptr, indices, last, seq, world: int) -
         lm.flashinfer, lm.paged_attention = saved
 
 
-def _traffic_from_profile(bytes_decode: int):
-    """DRAM bytes per decode launch from the committed ncu summary, if present."""
-    path = os.path.join(REPO, "profiles", "decode_kernel_traffic.json")
+def _traffic_from_profile(bytes_launch: int, head_dim: int, name="decode_kernel_traffic.json"):
+    """DRAM bytes per launch of the kernel instance for this head size, from
+    the committed ncu summary (None if none was captured): the capture's
+    bytes scaled by the algorithmic bytes of this launch over the capture's
+    (traffic grows with the K/V bytes processed)."""
+    path = os.path.join(REPO, "profiles", name)
     if not os.path.exists(path):
         return None
     with open(path) as f:
-        d = json.load(f)
-    # captured on a smaller case; traffic scales with the KV bytes processed
-    return int(d["dram_bytes_per_launch"] * bytes_decode / d["algorithmic_bytes_per_launch"])
+        d = json.load(f)["by_head_dim"].get(str(head_dim))
+    if d is None:
+        return None
+    return int(d["dram_bytes_per_launch"] * bytes_launch / d["algorithmic_bytes_per_launch"])
 
 
 # --------------------------------------------------------------- cfg3
-def run_mixed(args):
+def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
     """Configuration 3: one Llama-3-8B attention layer serving a mixed step —
     16 prefill chunks of 512 rows over cached prefixes U[0, 2048] (causal,
     tcgen05 prefill kernel) and 128 decode rows with contexts U[256, 4096]
     (decode kernel), both on the same pool. Requests are sharded round-robin
     (weak scaling: the whole mixed batch per GPU). value = decode GB/s of the
     step's decode part; the prefill part is reported as TFLOP/s of visible
-    (unmasked) query-key pairs."""
-    rank, world, local = _dist()
+    (unmasked) query-key pairs. Returns rank 0's line (None elsewhere)."""
+    rank, world, local = ctx
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     lir = importlib.import_module(PKG)
     fi, ours = _backend(args)
-    wl, geom, n_dec, lo, hi, layers, wname = _workload(args)
+    wl, geom, n_dec, lo, hi, layers, wname = _workload("cfg3")
     pre = wl.config3_prefill(seed=rank, device=dev)
     dec = wl.make_decode_problem(geom, n_dec, lo, hi, seed=100 + rank, device=dev, num_layers=1,
                                  append=False)
@@ -721,7 +827,7 @@ def run_mixed(args):
     stream = torch.cuda.current_stream()
     ev = []
 
-    def step(record):
+    def step(record, e=None):
         # total_qo (this package's extension) lets the prefill plan run on the
         # device without reading qo_indptr back; FlashInfer plans on the host
         extra = {"total_qo": q_pre.shape[0]} if ours else {}
@@ -729,16 +835,18 @@ def run_mixed(args):
                 causal=True, q_data_type=q_pre.dtype, **extra)
         dw.plan(dindptr, dindices, dlast, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim,
                 16, q_data_type=q_dec.dtype)
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if record else None
         if record:
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        if e is not None:
             e[0].record(stream)
         pw.run(q_pre, pre.pool[0], out=out_pre)
-        if record:
+        if e is not None:
             e[1].record(stream)
         dw.run(q_dec, dec.pool[0], out=out_dec)
-        if record:
+        if e is not None:
             e[2].record(stream)
-            ev.append(e)
+            if record:
+                ev.append(e)
 
     for _ in range(args.warmup):
         step(False)
@@ -760,26 +868,44 @@ def run_mixed(args):
         torch.cuda.synchronize()
         return t0.elapsed_time(t1)
 
-    # eager launches first (their events time the two kernels), then this
-    # package's step replayed from a CUDA graph (both plans run on the device)
+    # eager launches first, then this package's step replayed from a CUDA
+    # graph (both plans run on the device). The graph holds record nodes of
+    # three external events around the prefill and decode launches; after
+    # the timed replays the same graph is replayed once per step and the two
+    # kernels' durations are read from them (eager events for FlashInfer).
     eager_local = timed(lambda: step(True))
     graph = None
+    spans = []
     if ours and not args.eager:
+        ge = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            step(False)
+            step(False, ge)
         graph.replay()
         torch.cuda.synchronize()
         _barrier(world)
         ms_local = timed(graph.replay)
+        for _ in range(args.steps):
+            graph.replay()
+            torch.cuda.synchronize()
+            spans.append((ge[0].elapsed_time(ge[1]), ge[1].elapsed_time(ge[2])))
+        del graph
     else:
         ms_local = eager_local
     _barrier(world)
     clocks = sampler.stop()
     ms = _max_over_ranks(ms_local, world)
     eager_ms = _max_over_ranks(eager_local, world)
-    pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
-    dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    if spans:
+        pre_ms = statistics.mean(a for a, _ in spans)
+        dec_ms = statistics.mean(b for _, b in spans)
+        launch_timing = "event record nodes around each kernel inside the replayed step graph"
+    else:
+        pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+        dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+        launch_timing = "event pairs around each eager launch"
+    pre_ms = _max_over_ranks(pre_ms, world)
+    dec_ms = _max_over_ranks(dec_ms, world)
     _check(lir, ours, "bench cfg3")
     total_dbytes = _sum_over_ranks(float(dbytes) * args.steps, world)
     value = total_dbytes / (ms * 1e-3) / 1e9
@@ -857,9 +983,16 @@ def run_mixed(args):
     cpu, cpu_pre = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and ours:
         from oracle import cpu_baseline as cb
-        cpu = cb.time_decode_sample(dec.lengths, geom, budget_s=8.0, sample=16)
-        cpu_pre = cb.time_prefill_sample(pre.qo_lens, pre.prefix_lens, geom, budget_s=8.0)
+        cpu = cb.time_decode_sample(dec.lengths, geom, budget_s=cpu_budget_s, sample=16)
+        cpu_pre = cb.time_prefill_sample(pre.qo_lens, pre.prefix_lens, geom,
+                                         budget_s=cpu_budget_s)
+    pre_counters = _prefill_counters()
+    per_rank = _gather({"ms_per_step": round(ms_local / args.steps, 4),
+                        "prefill_tflops": round(pre_tf, 1),
+                        "decode_frac_of_hbm": round(dec_gbs / peak_bw, 4)}, world)
     _barrier(world)
+    del pre, dec, ws_p, ws_d
+    line = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -879,14 +1012,19 @@ def run_mixed(args):
                          "unit": "GB/s", "frac": round(dec_gbs / peak_bw, 4),
                          "peak_kind": bw_kind, "kernel": "decode_kernel",
                          "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_ms, 5),
-                         "traffic": None},
+                         "launch_timing": launch_timing,
+                         "traffic": _traffic_from_profile(dbytes, geom.head_dim) if ours
+                         else None},
             "prefill": {"tflops": round(pre_tf, 1), "gflop_per_launch": round(flops / 1e9, 2),
-                        "avg_launch_ms": round(pre_ms, 5),
+                        "avg_launch_ms": round(pre_ms, 5), "launch_timing": launch_timing,
                         "roofline": {"bound": "tensor", "achieved": round(pre_tf, 1),
                                      "peak": peak_tf, "unit": "TFLOP/s",
                                      "frac": round(pre_tf / peak_tf, 4),
                                      "peak_kind": "measured (cuBLAS bf16 burst)",
-                                     "kernel": "prefill_kernel"},
+                                     "kernel": "prefill_kernel",
+                                     "traffic": pre_counters.get("dram_bytes_per_launch")},
+                        "tensor_pipe_active": pre_counters.get("tensor_pipe_active"),
+                        "counters_source": pre_counters.get("source"),
                         "cpu_baseline": cpu_pre},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / args.steps, 4),
@@ -895,12 +1033,21 @@ def run_mixed(args):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if world > 1:
+            line["per_rank"] = per_rank
         if not ours:
             _mark_flashinfer(line)
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    return line
+
+
+def _prefill_counters() -> dict:
+    """The prefill kernel's ncu counters on configuration 3 (committed
+    summary), if captured: tensor-pipe activity and DRAM bytes per launch."""
+    path = os.path.join(REPO, "profiles", "prefill_kernel_counters.json")
+    if not os.path.exists(path):
+        return {}
+    with open(path) as f:
+        return json.load(f)
 
 
 # ------------------------------------------------------------- CPU side
@@ -913,38 +1060,45 @@ def cpu_baseline(prob_lengths: np.ndarray, geom, layers: int, budget_s: float = 
     return cb.time_decode_sample(prob_lengths, geom, budget_s=budget_s, sample=sample)
 
 
-def run_reference(args):
-    rank, world, local = _dist()
+def run_reference(args, ctx):
+    rank, world, local = ctx
     if rank != 0:
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-        return
-    wl, geom, per_gpu, lo, hi, layers, wname = _workload(args)
+        return None
+    workload = args.workload
+    wl, geom, per_gpu, lo, hi, layers, wname = _workload(workload)
     from oracle import cpu_baseline as cb
     lengths_all = _global_lengths(per_gpu * world, lo, hi)
     mine = wl.round_robin(per_gpu * world, world, 0)
-    res = cb.run_reference_arm(lengths_all[mine], geom, steps=args.steps, warmup=args.warmup)
+    lens = lengths_all[mine]
+    res = cb.run_reference_arm(lens, geom, steps=args.steps, warmup=args.warmup)
+    # the same config object as this package's line for the workload
+    bytes_decode = int(lens.sum()) * geom.kv_bytes_per_token + \
+        2 * len(lens) * geom.num_qo_heads * geom.head_dim * 2
+    l2 = ("inputs larger than L2 (KV of one layer "
+          f"{bytes_decode / 1e6:.0f} MB vs 126 MB L2)")
     line = {
         "metric": METRIC, "value": round(res["value"], 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded N(0,1) q/K/V, random page permutation",
-        "config": {"workload": wname, "layers": layers, "num_qo_heads": geom.num_qo_heads,
-                   "num_kv_heads": geom.num_kv_heads, "head_dim": geom.head_dim,
-                   "page_size": geom.page_size, "requests_per_gpu": per_gpu,
-                   "global_batch": per_gpu * world, "context": f"U[{lo},{hi}] + 1 appended",
-                   "parallelism": "host cores of rank 0"},
+        "config": _config(workload, geom, layers, per_gpu * world, world, lo, hi, l2),
         "impl": "reference",
         "cpu_baseline": {"value": round(res["value"], 3), "unit": "GB/s", "cores": res["cores"],
-                         "kind": "port", "sample": res["sample"]},
+                         "kind": "port", "sample": res["sample"] + "; host cores of rank 0"},
         "e2e": {"value": round(res["value"], 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+    return line
+
+
+# other configurations carried in the headline line: (key, workload, strong scaling)
+EXTRA = [("prefill_cfg3", "cfg3", False), ("long_cfg5", "cfg5", True),
+         ("cascade_cfg4", "cfg4", False), ("small_cfg1", "cfg1", False)]
+# keys of a configuration's own line kept in its sub-object
+SUB_KEYS = ("value", "unit", "ms_per_step", "scaling", "step_launch", "eager_ms_per_step",
+            "config", "decode_tok_s", "roofline", "prefill", "e2e", "cpu_baseline", "clocks",
+            "gpu_launches", "cascade", "unique_value", "unique_kv_bytes_per_layer",
+            "logical_kv_bytes_per_layer", "note", "per_rank")
 
 
 def main():
@@ -955,6 +1109,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference", "flashinfer"], default="ours")
     ap.add_argument("--workload", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"],
                     default="cfg2")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="measure the headline workload only (no other configurations)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the full-model decode step of configuration 2")
@@ -963,12 +1119,27 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
-        run_reference(args)
-    elif args.workload == "cfg3":
-        run_mixed(args)
-    else:
-        run_ours(args)
+    ctx = _dist()
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, ctx)
+        elif args.workload == "cfg3":
+            line = run_mixed(args, ctx)
+        else:
+            line = run_ours(args, ctx, args.workload, strong=args.workload == "cfg5")
+        if (args.workload == "cfg2" and args.impl == "ours" and not args.headline_only):
+            for key, workload, strong in EXTRA:
+                torch.cuda.empty_cache()
+                sub = (run_mixed(args, ctx, cpu_budget_s=5.0) if workload == "cfg3" else
+                       run_ours(args, ctx, workload, strong=strong, cpu_budget_s=5.0))
+                if line is not None:
+                    line[key] = {k: sub[k] for k in SUB_KEYS if k in sub}
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if ctx[1] > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -57,6 +57,7 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
     # timed-region reductions as bench.py does them
     t_max = bench._max_over_ranks(float(rank + 1), w)
     t_sum = bench._sum_over_ranks(float(len(mine)), w)
+    per_rank = bench._gather({"rank": r, "requests": len(mine)}, w)
     bench._barrier(w)
     gathered = [None] * w
     dist.all_gather_object(gathered, (mine.tolist(), out.numpy(), prob.pool[0].numpy(),
@@ -65,6 +66,7 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
     if rank == 0:
         np.save(os.path.join(result_dir, "meta.npy"),
                 np.array([t_max, t_sum, per_gpu * w], dtype=np.float64))
+        assert per_rank == [{"rank": i, "requests": per_gpu} for i in range(w)]
         torch.save({"gathered": gathered, "q_all": q_all, "lengths": lengths_all},
                    os.path.join(result_dir, "gathered.pt"))
     dist.destroy_process_group()
@@ -109,3 +111,16 @@ def test_reference_arm_runs_on_rank_zero_only(tmp_path):
     import json
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["cpu_baseline"]["kind"] == "port"
+
+
+def test_reference_arm_reports_the_same_config_as_this_package():
+    """The reference arm's config object is built by the same function as
+    this package's line for the workload, so the keys and the values that
+    describe the workload agree."""
+    bench = importlib.import_module("bench")
+    wl, geom, per_gpu, lo, hi, layers, _ = bench._workload("cfg2")
+    cfg = bench._config("cfg2", geom, layers, per_gpu, 1, lo, hi, "x")
+    assert cfg["global_batch"] == 256 and cfg["requests_per_gpu"] == 256
+    assert cfg["parallelism"] == "request-sharded x1, no collective"
+    strong = bench._config("cfg5", wl.LLAMA3_8B, 1, 512, 8, 8192, 32768, "x", strong=True)
+    assert strong["global_batch"] == 512 and strong["requests_per_gpu"] == 64
