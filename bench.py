@@ -355,6 +355,9 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
     if ours and not args.eager:
         gspan = (torch.cuda.Event(enable_timing=True, external=True),
                  torch.cuda.Event(enable_timing=True, external=True))
+        for e in gspan:  # create the events outside the capture
+            e.record(stream)
+        torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step(False, span=gspan)
@@ -878,6 +881,9 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
     spans = []
     if ours and not args.eager:
         ge = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+        for e in ge:  # create the events outside the capture
+            e.record(stream)
+        torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             step(False, ge)
