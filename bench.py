@@ -267,10 +267,20 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
     stream = torch.cuda.current_stream()
     dec_events = []
 
-    def step(record: bool, span=None):
-        bi, pos = fi.get_batch_indices_positions(append_indptr, seq, B)
+    state = {}
+
+    def prologue():
+        state["bi"], state["pos"] = fi.get_batch_indices_positions(append_indptr, seq, B)
         wrap.plan(indptr, indices, last, geom.num_qo_heads, geom.num_kv_heads, geom.head_dim,
                   P, q_data_type=q.dtype)
+
+    def decode_layers():
+        for layer in range(layers):
+            wrap.run_with_append(q, pool[layer], k_new, v_new, state["pos"], out=out)
+
+    def step(record: bool, span=None):
+        prologue()
+        bi, pos = state["bi"], state["pos"]
         # Decode-kernel timing: this package's layers are back-to-back decode
         # launches, timed as one span per step (events between them would
         # stop each launch from overlapping its predecessor's tail) and
@@ -342,37 +352,48 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
 
     # Eager launches first, then -- this package only -- the same step
     # captured once in a CUDA graph and replayed, which is how a serving loop
-    # runs a launch-bound decode step. The graph holds one event pair around
-    # its decode launches (record nodes of external events): after the timed
-    # replays, the same graph is replayed once per step with a read of that
-    # span, which gives the decode kernel's duration for the roofline inside
-    # the step that value times. FlashInfer's plan works on the host and
-    # cannot be captured, so its arm stays eager and its decode launches are
-    # timed one by one.
+    # runs a launch-bound decode step. The decode kernel's duration for the
+    # roofline comes from a second graph holding only the step's decode
+    # launches (the prologue's plan stays valid in the workspace), replayed
+    # back to back with an event between replays (one per replay after an
+    # L2 flush for the configurations that fit in L2): the step's launches
+    # as the timed step runs them, without its prologue. FlashInfer's plan works on the host
+    # and cannot be captured, so its arm stays eager and its decode launches
+    # are timed one by one.
     eager_local = timed(lambda: step(True))
-    graph = None
     spans = []
     if ours and not args.eager:
-        gspan = (torch.cuda.Event(enable_timing=True, external=True),
-                 torch.cuda.Event(enable_timing=True, external=True))
-        for e in gspan:  # create the events outside the capture
-            e.record(stream)
-        torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            step(False, span=gspan)
+            step(False)
         graph.replay()
         torch.cuda.synchronize()
         _barrier(world)
         ms_local = timed(graph.replay)
+        dgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(dgraph):
+            decode_layers()
+        dgraph.replay()
+        torch.cuda.synchronize()
         _barrier(world)
         if small:
-            timed(graph.replay, after=lambda: spans.append(gspan[0].elapsed_time(gspan[1])))
-        else:
             for _ in range(args.steps):
-                graph.replay()
+                flush.view(torch.int64).sum()
+                t0.record(stream)
+                dgraph.replay()
+                t1.record(stream)
                 torch.cuda.synchronize()
-                spans.append(gspan[0].elapsed_time(gspan[1]))
+                spans.append(t0.elapsed_time(t1))
+        else:
+            # back to back, one event between replays, read after one sync
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+            evs[0].record(stream)
+            for k in range(args.steps):
+                dgraph.replay()
+                evs[k + 1].record(stream)
+            torch.cuda.synchronize()
+            spans = [evs[k].elapsed_time(evs[k + 1]) for k in range(args.steps)]
+        del graph, dgraph
     else:
         ms_local = eager_local
     _barrier(world)
@@ -381,7 +402,8 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
     eager_ms = _max_over_ranks(eager_local, world)
     if spans:
         dec_ms_local = statistics.mean(spans) / layers
-        dec_timing = "one event span around the decode launches inside the replayed step graph"
+        dec_timing = ("one event span around a graph of the step's decode launches, "
+                      "replayed back to back as in the step graph")
     else:
         dec_ms_local = (sum(a.elapsed_time(b) for a, b, _ in dec_events)
                         / sum(n for _, _, n in dec_events))
@@ -391,8 +413,6 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
     value = total_bytes / (ms * 1e-3) / 1e9
     tok_s = _sum_over_ranks(float(B) * args.steps, world) / (ms * 1e-3)
     _check(lir, ours, f"bench {workload} timed region")
-    if graph is not None:
-        del graph
 
     # ---- end to end through the public API from pinned host memory
     # Every step copies its inputs in (tables once, then each layer's q and new
@@ -830,7 +850,8 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
     stream = torch.cuda.current_stream()
     ev = []
 
-    def step(record, e=None):
+    def step(record):
+        e = None
         # total_qo (this package's extension) lets the prefill plan run on the
         # device without reading qo_indptr back; FlashInfer plans on the host
         extra = {"total_qo": q_pre.shape[0]} if ours else {}
@@ -872,30 +893,41 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
         return t0.elapsed_time(t1)
 
     # eager launches first, then this package's step replayed from a CUDA
-    # graph (both plans run on the device). The graph holds record nodes of
-    # three external events around the prefill and decode launches; after
-    # the timed replays the same graph is replayed once per step and the two
-    # kernels' durations are read from them (eager events for FlashInfer).
+    # graph (both plans run on the device). The two kernels' durations come
+    # from two more graphs, the step's prefill launch and its decode launch
+    # (the plans stay valid in the workspaces), replayed one after the other
+    # between events, in the step's order (eager events for FlashInfer).
     eager_local = timed(lambda: step(True))
     graph = None
     spans = []
     if ours and not args.eager:
-        ge = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
-        for e in ge:  # create the events outside the capture
-            e.record(stream)
-        torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            step(False, ge)
+            step(False)
         graph.replay()
         torch.cuda.synchronize()
         _barrier(world)
         ms_local = timed(graph.replay)
-        for _ in range(args.steps):
-            graph.replay()
-            torch.cuda.synchronize()
-            spans.append((ge[0].elapsed_time(ge[1]), ge[1].elapsed_time(ge[2])))
-        del graph
+        gp, gd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gp):
+            pw.run(q_pre, pre.pool[0], out=out_pre)
+        with torch.cuda.graph(gd):
+            dw.run(q_dec, dec.pool[0], out=out_dec)
+        gp.replay()
+        gd.replay()
+        torch.cuda.synchronize()
+        # back to back, events between the replays, read after one sync
+        ge = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
+        ge[0].record(stream)
+        for k in range(args.steps):
+            gp.replay()
+            ge[2 * k + 1].record(stream)
+            gd.replay()
+            ge[2 * k + 2].record(stream)
+        torch.cuda.synchronize()
+        spans = [(ge[2 * k].elapsed_time(ge[2 * k + 1]), ge[2 * k + 1].elapsed_time(ge[2 * k + 2]))
+                 for k in range(args.steps)]
+        del graph, gp, gd
     else:
         ms_local = eager_local
     _barrier(world)
@@ -905,7 +937,7 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
     if spans:
         pre_ms = statistics.mean(a for a, _ in spans)
         dec_ms = statistics.mean(b for _, b in spans)
-        launch_timing = "event record nodes around each kernel inside the replayed step graph"
+        launch_timing = "events around graphs of the step's prefill and decode launches"
     else:
         pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
         dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
@@ -1006,7 +1038,7 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) q/K/V, random page permutation",
-            "step_launch": "CUDA graph replay" if graph is not None else "eager",
+            "step_launch": "CUDA graph replay" if spans else "eager",
             "eager_ms_per_step": round(eager_ms / args.steps, 4),
             "config": {"workload": wname, "layers": 1, "num_qo_heads": geom.num_qo_heads,
                        "num_kv_heads": geom.num_kv_heads, "head_dim": geom.head_dim,
