@@ -377,20 +377,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc_s = umma_idesc_f16(ab, kPfRows, kPfKeys, 0);
       const uint32_t idesc_o = umma_idesc_f16(ab, kPfRows, D, 1);
-      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
+      // Shared-memory descriptors are formed once: a descriptor's address
+      // field is the byte address / 16 (all of shared memory fits its 14
+      // bits), so stepping through an operand is one add of a constant.
+      // Between hand-offs the issuing thread then runs little more than the
+      // MMAs themselves: it shares its sub-partition's issue slots with two
+      // softmax warps, and every slot it waits for leaves the tensor pipe's
+      // short queue emptier.
+      const uint64_t dq0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
+      const uint64_t dk0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
+      const uint64_t dv0 = umma_desc_sw128(smem_u32(sV), C::kPanelBytes, 1024);
+      constexpr uint64_t kQStep = C::kQBytes >> 4, kTileStep = C::kTileBytes >> 4;
       if (!mbar_wait_warp(q_full, 0)) failed = true;
       // S_t = Q_t K_j^T into TMEM columns [128 t, 128 t + 128); lane 0 only
       auto issue_s = [&](int t, int j) {
-        const int st = j % S;
+        const uint64_t dq = dq0 + t * kQStep, dk = dk0 + (j % S) * kTileStep;
+        const uint32_t d = tmem + t * kPfKeys;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::kPanelBytes + (kk & 3) * 32;
-          umma_f16(tmem + t * kPfKeys, umma_desc_sw128(q_base + t * C::kQBytes + off, 16, 1024),
-                   umma_desc_sw128(k_base + st * C::kTileBytes + off, 16, 1024), idesc_s,
-                   kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * C::kPanelBytes + (kk & 3) * 32) >> 4;
+          umma_f16(d, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[t]);
-        if (t == 1) umma_commit(&k_empty[st]);
+        if (t == 1) umma_commit(&k_empty[j % S]);
       };
       named_bar_sync(kPfBarK, kPfBarKVThreads);
       if (lane == 0) {
@@ -401,13 +410,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       for (int j = 0; j < ntiles; ++j) {
         const int st = j % S;
+        const uint64_t dv = dv0 + st * kTileStep;
         named_bar_sync(kPfBarV, kPfBarKVThreads);
+#pragma unroll
         for (int t = 0; t < 2; ++t) {
           named_bar_sync(kPfBarP + t, kPfBarPThreads);
           if (t == 0 && j + 1 < ntiles) named_bar_sync(kPfBarK, kPfBarKVThreads);
           if (lane == 0) {
             tc_fence_after();
             // O_t += P_t V_j; P_t: TMEM columns [128 t, 128 t + 64), 16 keys per 8 columns
+            const uint32_t d = tmem + 256 + t * D, pa = tmem + t * kPfKeys;
 #pragma unroll
             for (int kk = 0; kk < kPfKeys / 16; ++kk) {
               asm volatile(
@@ -415,11 +427,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                   "  .reg .pred p;\n"
                   "  setp.ne.b32 p, %4, 0;\n"
                   "  tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
-                  "}\n" ::"r"(tmem + 256 + t * D),
-                  "r"(tmem + t * kPfKeys + kk * 8),
-                  "l"(umma_desc_sw128(v_base + st * C::kTileBytes + kk * 2048, C::kPanelBytes,
-                                      1024)),
-                  "r"(idesc_o), "r"((j > 0 || kk > 0) ? 1u : 0u)
+                  "}\n" ::"r"(d),
+                  "r"(pa + kk * 8), "l"(dv + ((kk * 2048) >> 4)), "r"(idesc_o),
+                  "r"((j > 0 || kk > 0) ? 1u : 0u)
                   : "memory");
             }
             umma_commit(&o_done[t]);
