@@ -84,7 +84,8 @@ def _dist():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        # short: ranks that wait for one another end with an error, not a hang
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=180))
     return rank, world, local
 
 
@@ -561,6 +562,9 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
     if rank == 0 and world == 1 and not args.no_cpu_baseline and ours:
         cpu = cpu_baseline(prob_lengths=prob.lengths, geom=geom, layers=layers,
                            budget_s=cpu_budget_s)
+    # every collective of this workload before rank 0 alone builds the line
+    unique_total = (_sum_over_ranks(float(layers * unique_kv) * args.steps, world)
+                    if workload == "cfg4" else 0.0)
     _barrier(world)
     del prob, pool, ws, flush
     if rank != 0:
@@ -581,8 +585,7 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
         "decode_tok_s": round(tok_s, 1),
         **({"unique_kv_bytes_per_layer": int(unique_kv),
             "logical_kv_bytes_per_layer": int(bytes_decode),
-            "unique_value": round(_sum_over_ranks(float(layers * unique_kv) * args.steps, world)
-                                  / (ms * 1e-3) / 1e9, 2),
+            "unique_value": round(unique_total / (ms * 1e-3) / 1e9, 2),
             "note": "value counts the shared prefix once per request (logical bytes); its "
                     "pages stay in L2, so logical GB/s can exceed the HBM peak; unique_value "
                     "counts every distinct page once"}
