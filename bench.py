@@ -409,7 +409,10 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
         dec_ms_local = (sum(a.elapsed_time(b) for a, b, _ in dec_events)
                         / sum(n for _, _, n in dec_events))
         dec_timing = "event pairs around each eager decode launch"
-    dec_ms = _max_over_ranks(dec_ms_local, world)
+    # ranks decode different requests: the line's kernel figures are the mean
+    # over ranks of the bytes per launch and of the launch duration (the
+    # slowest rank's step time is in ms_per_step; per_rank lists each rank)
+    dec_ms = _sum_over_ranks(dec_ms_local, world) / world
     total_bytes = _sum_over_ranks(float(bytes_step) * args.steps, world)
     value = total_bytes / (ms * 1e-3) / 1e9
     tok_s = _sum_over_ranks(float(B) * args.steps, world) / (ms * 1e-3)
@@ -550,11 +553,12 @@ def run_ours(args, ctx, workload: str, strong: bool = False, cpu_budget_s: float
 
     peak, peak_kind = _peaks()
     # the timed launch: decode + the step's fused append (ours), decode alone (FlashInfer)
-    bytes_launch = bytes_decode + (bytes_append if ours else 0)
+    bytes_launch_local = bytes_decode + (bytes_append if ours else 0)
+    bytes_launch = int(round(_sum_over_ranks(float(bytes_launch_local), world) / world))
     achieved = bytes_launch / (dec_ms * 1e-3) / 1e9
     per_rank = _gather({"ms_per_step": round(ms_local / args.steps, 4),
-                        "decode_frac_of_hbm": round(bytes_launch / (dec_ms_local * 1e-3) / 1e9
-                                                    / peak, 4),
+                        "decode_frac_of_hbm": round(bytes_launch_local / (dec_ms_local * 1e-3)
+                                                    / 1e9 / peak, 4),
                         "e2e_gbs": round(bytes_step * args.steps / (e2e_local * 1e-3) / 1e9, 1),
                         "h2d_gbs": round(h2d_gbs, 2), "d2h_gbs": round(d2h_gbs, 2),
                         "requests": B}, world)
@@ -945,8 +949,13 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
         pre_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
         dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
         launch_timing = "event pairs around each eager launch"
-    pre_ms = _max_over_ranks(pre_ms, world)
-    dec_ms = _max_over_ranks(dec_ms, world)
+    # mean over ranks (each rank serves its own mixed batch), as in run_ours
+    pre_ms_local, dec_ms_local = pre_ms, dec_ms
+    pre_ms = _sum_over_ranks(pre_ms, world) / world
+    dec_ms = _sum_over_ranks(dec_ms, world) / world
+    flops_local, dbytes_local = flops, dbytes
+    flops = _sum_over_ranks(float(flops), world) / world
+    dbytes = int(round(_sum_over_ranks(float(dbytes), world) / world))
     _check(lir, ours, "bench cfg3")
     total_dbytes = _sum_over_ranks(float(dbytes) * args.steps, world)
     value = total_dbytes / (ms * 1e-3) / 1e9
@@ -1029,8 +1038,9 @@ def run_mixed(args, ctx, cpu_budget_s: float = 8.0):
                                          budget_s=cpu_budget_s)
     pre_counters = _prefill_counters()
     per_rank = _gather({"ms_per_step": round(ms_local / args.steps, 4),
-                        "prefill_tflops": round(pre_tf, 1),
-                        "decode_frac_of_hbm": round(dec_gbs / peak_bw, 4)}, world)
+                        "prefill_tflops": round(flops_local / (pre_ms_local * 1e-3) / 1e12, 1),
+                        "decode_frac_of_hbm": round(dbytes_local / (dec_ms_local * 1e-3) / 1e9
+                                                    / peak_bw, 4)}, world)
     _barrier(world)
     del pre, dec, ws_p, ws_d
     line = None
