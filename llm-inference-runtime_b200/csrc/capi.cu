@@ -645,17 +645,17 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
   };
   static std::atomic<uint64_t> done[8];
   using N6 = QkvCfg<128, 6>;
-  using W3 = QkvCfg<256, 3>;
+  using W2 = QkvCfg<256, 2>;
   if (bf && D == 64)
-    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 64, 256, 3>, W3::kSmemBytes, &done[0])
+    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 64, 256, 2>, W2::kSmemBytes, &done[0])
                 : go(qkv_rope_append_kernel<__nv_bfloat16, 64, 128, 6>, N6::kSmemBytes, &done[1]);
   if (bf)
-    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 128, 256, 3>, W3::kSmemBytes, &done[2])
+    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 128, 256, 2>, W2::kSmemBytes, &done[2])
                 : go(qkv_rope_append_kernel<__nv_bfloat16, 128, 128, 6>, N6::kSmemBytes, &done[3]);
   if (D == 64)
-    return wide ? go(qkv_rope_append_kernel<__half, 64, 256, 3>, W3::kSmemBytes, &done[4])
+    return wide ? go(qkv_rope_append_kernel<__half, 64, 256, 2>, W2::kSmemBytes, &done[4])
                 : go(qkv_rope_append_kernel<__half, 64, 128, 6>, N6::kSmemBytes, &done[5]);
-  return wide ? go(qkv_rope_append_kernel<__half, 128, 256, 3>, W3::kSmemBytes, &done[6])
+  return wide ? go(qkv_rope_append_kernel<__half, 128, 256, 2>, W2::kSmemBytes, &done[6])
               : go(qkv_rope_append_kernel<__half, 128, 128, 6>, N6::kSmemBytes, &done[7]);
 }
 

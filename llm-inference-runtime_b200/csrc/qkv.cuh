@@ -30,7 +30,9 @@ constexpr int kQkvThreads = 192;
 // Tile shapes: N=128 columns with a deep 6-stage ring for few tokens (the
 // GEMM then streams the weight: more CTAs, more bytes in flight per CTA);
 // N=256 columns for many tokens (MMAs of 128 cycles keep the issuer's
-// per-stage barrier wait hidden behind the queued MMAs).
+// per-stage barrier wait hidden behind the queued MMAs) with a 2-stage
+// ring, so that two CTAs share an SM (96 KB of shared memory and 256 TMEM
+// columns each) and one CTA's epilogue runs under the other's main loop.
 template <int BN, int STAGES>
 struct QkvCfg {
   static constexpr int kStageBytes = (kQkvBM + BN) * kQkvBK * 2;
@@ -80,7 +82,7 @@ __device__ __forceinline__ int64_t qkv_slot(const QkvParams& p, int m, int h) {
 }
 
 template <typename T, int D, int BN, int STAGES>
-__global__ void __launch_bounds__(kQkvThreads, 1)
+__global__ void __launch_bounds__(kQkvThreads, 2)
     qkv_rope_append_kernel(const __grid_constant__ CUtensorMap xmap,
                            const __grid_constant__ CUtensorMap wmap, const QkvParams p) {
   constexpr int S = STAGES;
