@@ -103,10 +103,13 @@ __global__ void append_kernel(const AppendParams p) {
 // fp32 math, result rounded to T. The standalone kernel and the fused
 // RoPE + append kernel share these two functions (no FMA contraction), so
 // both paths give bit-identical rows.
+__device__ __forceinline__ float rope_freq(int i, int rotary_dim, float inv_scale,
+                                          float log2_theta) {
+  return exp2f(-(2.0f * i / rotary_dim) * log2_theta) * inv_scale;
+}
 __device__ __forceinline__ void rope_cos_sin(int pos, int i, int rotary_dim, float inv_scale,
                                              float log2_theta, float* cs, float* sn) {
-  const float freq = exp2f(-(2.0f * i / rotary_dim) * log2_theta) * inv_scale;
-  sincosf(static_cast<float>(pos) * freq, sn, cs);
+  sincosf(static_cast<float>(pos) * rope_freq(i, rotary_dim, inv_scale, log2_theta), sn, cs);
 }
 __device__ __forceinline__ void rope_rotate(float x0, float x1, float cs, float sn, float* y0,
                                             float* y1) {

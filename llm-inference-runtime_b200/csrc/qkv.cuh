@@ -33,10 +33,18 @@ constexpr int kQkvThreads = 192;
 // per-stage barrier wait hidden behind the queued MMAs) with a 2-stage
 // ring, so that two CTAs share an SM (96 KB of shared memory and 256 TMEM
 // columns each) and one CTA's epilogue runs under the other's main loop.
+//
+// RoPE cos / sin of each (token, pair): with N=128 tiles (one CTA per SM)
+// the epilogue warps tabulate them in TMEM columns [128, 256) while the main
+// loop runs (cos of pair i in column 128 + i, sin in 192 + i); with N=256
+// tiles TMEM is full, so they go to the released stage memory after it.
+// Either way the pair frequencies are computed once per CTA (smem).
 template <int BN, int STAGES>
 struct QkvCfg {
   static constexpr int kStageBytes = (kQkvBM + BN) * kQkvBK * 2;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + 256 + 1024;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + 512 + 1024;
+  static constexpr bool kTabTmem = BN == 128;
+  static constexpr int kTmemCols = 256;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -87,12 +95,15 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
                            const __grid_constant__ CUtensorMap wmap, const QkvParams p) {
   constexpr int S = STAGES;
   constexpr int kStageBytes = QkvCfg<BN, STAGES>::kStageBytes;
+  constexpr bool kTabTmem = QkvCfg<BN, STAGES>::kTabTmem;
+  constexpr int kTmemCols = QkvCfg<BN, STAGES>::kTmemCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  float* freq = reinterpret_cast<float*>(smem + S * kStageBytes + 256);  // [rotary_dim / 2]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kQkvBM, n0 = blockIdx.y * BN;
   const int nk = p.K / kQkvBK;
@@ -108,7 +119,7 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
     fence_mbar_init();
   }
   if (warp == 5) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -163,73 +174,129 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
     const int r = warp * 32 + lane;  // tile row == TMEM lane
     const int m = m0 + r;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    constexpr int HPT = BN / D;  // heads per tile
+    const int qcols = p.hq * D, kcols = p.hkv * D;
+    const int region = n0 < qcols ? 0 : (n0 < qcols + kcols ? 1 : 2);  // q / k / v
+    const int head0 = region == 0 ? n0 / D : (region == 1 ? (n0 - qcols) / D
+                                                           : (n0 - qcols - kcols) / D);
+    const bool active = m < p.M;
+    const int half = p.rotary_dim / 2;
+    // Page slots of this row's k / v heads, looked up (three dependent
+    // global loads) while the main loop runs.
+    int64_t slot[HPT];
+#pragma unroll
+    for (int hh = 0; hh < HPT; ++hh)
+      slot[hh] = (active && region > 0) ? qkv_slot(p, m, head0 + hh) : -1;
+    const int pos = active ? __ldg(p.positions + m) : 0;
+    if (threadIdx.x < half) freq[threadIdx.x] = rope_freq(threadIdx.x, p.rotary_dim, p.inv_scale,
+                                                          p.log2_theta);
+    named_bar_sync(1, 128);  // the four epilogue warps
+    __syncwarp();  // tcgen05.ld / st below are warp-collective
+    // cos / sin of pairs [i0, i0 + 16) of this row: computed, and stored to
+    // TMEM columns or to the row's column of the shared-memory table
+    float* tab = reinterpret_cast<float*>(smem);
+    auto tabulate = [&](int i0) {
+      float cs[16], sn[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int i = min(i0 + u, half - 1);
+        sincosf(static_cast<float>(pos) * freq[i], &sn[u], &cs[u]);
+      }
+      if constexpr (kTabTmem) {
+        tmem_st16(taddr + BN + i0, cs);
+        tmem_st16(taddr + BN + 64 + i0, sn);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          if (i0 + u < half) {
+            tab[(i0 + u) * kQkvBM + r] = cs[u];
+            tab[(half + i0 + u) * kQkvBM + r] = sn[u];
+          }
+        }
+      }
+    };
+    auto table = [&](int i0, float* cs, float* sn) {
+      if constexpr (kTabTmem) {
+        tmem_ld16(taddr + BN + i0, cs);
+        tmem_ld16(taddr + BN + 64 + i0, sn);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int i = min(i0 + u, half - 1);
+          cs[u] = tab[i * kQkvBM + r];
+          sn[u] = tab[(half + i) * kQkvBM + r];
+        }
+      }
+    };
+    if constexpr (kTabTmem) {
+      if (region < 2) {
+#pragma unroll 1
+        for (int i0 = 0; i0 < half; i0 += 16) tabulate(i0);
+        tmem_wait_st();
+      }
+    }
     const bool ok = mbar_wait_warp(acc_full, 0);
     if (!ok) {
       if (lane == 0) set_status(PA_ERR_TIMEOUT);
     } else {
       tc_fence_after();
-      constexpr int HPT = BN / D;  // heads per tile
-      const int qcols = p.hq * D, kcols = p.hkv * D;
-      const int region = n0 < qcols ? 0 : (n0 < qcols + kcols ? 1 : 2);  // q / k / v
-      const int head0 = region == 0 ? n0 / D : (region == 1 ? (n0 - qcols) / D
-                                                             : (n0 - qcols - kcols) / D);
-      const int pos = m < p.M ? __ldg(p.positions + m) : 0;
-      const bool active = m < p.M;
-      // RoPE angles depend on (position, pair) only: each thread tabulates
-      // cos / sin for its token once, in the stage memory the main loop no
-      // longer needs (column r of [2 * half][128] floats, read back only by
-      // this thread), and every q / k head of the tile reuses them. Code
-      // that runs once per CTA stays small: the epilogue is instruction-
-      // fetch bound when straight-line.
-      float* tab = reinterpret_cast<float*>(smem);
-      const int half = p.rotary_dim / 2;
-      if (region < 2) {
+      if constexpr (!kTabTmem) {
+        // in the stage memory the main loop has released: column r of
+        // [2 * half][128] floats, read back only by this thread
+        if (region < 2) {
 #pragma unroll 1
-        for (int i = 0; i < half; ++i) {
-          float cs, sn;
-          rope_cos_sin(pos, i, p.rotary_dim, p.inv_scale, p.log2_theta, &cs, &sn);
-          tab[i * kQkvBM + r] = cs;
-          tab[(half + i) * kQkvBM + r] = sn;
+          for (int i0 = 0; i0 < half; i0 += 16) tabulate(i0);
         }
       }
 #pragma unroll 1
       for (int hh = 0; hh < HPT; ++hh) {
         float a[D];
+        __syncwarp();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) tmem_ld32(taddr + hh * D + c * 32, a + c * 32);
         tmem_wait_ld();
-        if (region < 2 && active) {
-          // fp32 rotation of the accumulator (rope_rotate, as rope_kernel)
+        if (region < 2) {
+          // fp32 rotation of the accumulator (rope_rotate, as rope_kernel),
+          // 16 pairs per table read; padding rows too (nothing stores them),
+          // since the TMEM table loads are warp-collective
           if (p.rotary_dim == D && !p.interleave) {
 #pragma unroll
-            for (int i = 0; i < D / 2; ++i) {
-              float y0, y1;
-              rope_rotate(a[i], a[i + D / 2], tab[i * kQkvBM + r], tab[(D / 2 + i) * kQkvBM + r],
-                          &y0, &y1);
-              a[i] = y0;
-              a[i + D / 2] = y1;
+            for (int i0 = 0; i0 < D / 2; i0 += 16) {
+              float cs[16], sn[16];
+              table(i0, cs, sn);
+#pragma unroll
+              for (int u = 0; u < 16; ++u)
+                rope_rotate(a[i0 + u], a[i0 + u + D / 2], cs[u], sn[u], &a[i0 + u],
+                            &a[i0 + u + D / 2]);
             }
           } else if (p.rotary_dim == D) {
 #pragma unroll
-            for (int i = 0; i < D / 2; ++i) {
-              float y0, y1;
-              rope_rotate(a[2 * i], a[2 * i + 1], tab[i * kQkvBM + r],
-                          tab[(D / 2 + i) * kQkvBM + r], &y0, &y1);
-              a[2 * i] = y0;
-              a[2 * i + 1] = y1;
+            for (int i0 = 0; i0 < D / 2; i0 += 16) {
+              float cs[16], sn[16];
+              table(i0, cs, sn);
+#pragma unroll
+              for (int u = 0; u < 16; ++u)
+                rope_rotate(a[2 * (i0 + u)], a[2 * (i0 + u) + 1], cs[u], sn[u], &a[2 * (i0 + u)],
+                            &a[2 * (i0 + u) + 1]);
             }
           } else {
             float tmp[D];
 #pragma unroll
             for (int e = 0; e < D; ++e) tmp[e] = a[e];
 #pragma unroll 1
-            for (int i = 0; i < half; ++i) {
-              float y0, y1;
-              const int ia = p.interleave ? 2 * i : i, ib = p.interleave ? 2 * i + 1 : i + half;
-              rope_rotate(tmp[ia], tmp[ib], tab[i * kQkvBM + r], tab[(half + i) * kQkvBM + r],
-                          &y0, &y1);
-              tmp[ia] = y0;
-              tmp[ib] = y1;
+            for (int i0 = 0; i0 < half; i0 += 16) {
+              float cs[16], sn[16];
+              table(i0, cs, sn);
+#pragma unroll 1
+              for (int u = 0; u < 16 && i0 + u < half; ++u) {
+                const int i = i0 + u;
+                const int ia = p.interleave ? 2 * i : i, ib = p.interleave ? 2 * i + 1 : i + half;
+                float y0, y1;
+                rope_rotate(tmp[ia], tmp[ib], cs[u], sn[u], &y0, &y1);
+                tmp[ia] = y0;
+                tmp[ib] = y1;
+              }
             }
 #pragma unroll
             for (int e = 0; e < D; ++e) a[e] = tmp[e];
@@ -241,9 +308,8 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
         uint8_t* dst = nullptr;
         if (active && region == 0) {
           dst = p.q_out + m * p.q_sn + static_cast<int64_t>(head0 + hh) * D * 2;
-        } else if (active) {
-          const int64_t off = qkv_slot(p, m, head0 + hh);
-          if (off >= 0) dst = (region == 1 ? p.k_base : p.v_base) + off;
+        } else if (slot[hh] >= 0) {
+          dst = (region == 1 ? p.k_base : p.v_base) + slot[hh];
         }
         if (dst != nullptr) {
 #pragma unroll
@@ -260,7 +326,7 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 

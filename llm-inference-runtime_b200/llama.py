@@ -30,8 +30,8 @@ from . import fused
 
 # The fused QKV projection kernel (one launch: GEMM + RoPE + KV append) is
 # opt-in: on a B200 it loses to cuBLAS + the fused RoPE/append kernel in GPU
-# time at decode sizes (19-33 vs 10-13 us) and is on par at 8192 tokens
-# (375 vs 340-382 us) while saving one launch. PA_FUSED_QKV=1 turns it on.
+# time at decode sizes (15-25 vs 10-13 us) and is on par at 8192 tokens
+# (374-387 vs 372-397 us) while saving one launch. PA_FUSED_QKV=1 turns it on.
 _FUSED_QKV = os.environ.get("PA_FUSED_QKV", "0") == "1"
 
 
