@@ -635,28 +635,76 @@ int pa_qkv_rope_append(const void* x, int64_t x_stride, const void* weight, int6
   const int bn = wide ? 256 : 128;
   rc = encode_2d_map(&wm, weight, N, hidden, w_stride, bn, cache->dtype);
   if (rc != PA_OK) return rc;
-  const dim3 grid(static_cast<unsigned>((num_tokens + kQkvBM - 1) / kQkvBM),
-                  static_cast<unsigned>(N / bn));
+  const int mt = (num_tokens + kQkvBM - 1) / kQkvBM, nt = static_cast<int>(N / bn);
+  const dim3 grid(static_cast<unsigned>(mt), static_cast<unsigned>(nt));
   const bool bf = cache->dtype == PA_DTYPE_BF16;
+  p.splits = 1;
   auto go = [&](auto kernel, int smem, std::atomic<uint64_t>* done) -> int {
     if (allow_smem(kernel, smem, done, dev) != cudaSuccess) return PA_ERR_CUDA;
     kernel<<<grid, kQkvThreads, smem, st>>>(xm, wm, p);
     return launch_status();
   };
-  static std::atomic<uint64_t> done[8];
+  // Few tiles (decode-sized batches): split K over a cluster of 2-4 CTAs
+  // per tile so that the weight streams through (nearly) every SM, as long
+  // as every cluster fits on the GPU at once.
+  auto go_split = [&](auto kernel, std::atomic<uint64_t>* done, int vi) -> int {
+    using SK = QkvCfg<128, 5, true>;
+    if (allow_smem(kernel, SK::kSmemBytes, done, dev) != cudaSuccess) return PA_ERR_CUDA;
+    static std::atomic<int> fits[4][5];  // clusters resident at once, by variant and size; 0 = unknown
+    const int sms = sm_count(dev) > 0 ? sm_count(dev) : 148;
+    int splits = std::min(4, sms / (mt * nt));
+    while (splits > 1 && hidden / kQkvBK < 4 * splits) --splits;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    cfg.blockDim = dim3(kQkvThreads);
+    cfg.dynamicSmemBytes = SK::kSmemBytes;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    for (; splits > 1; --splits) {
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = static_cast<unsigned>(splits);
+      cfg.gridDim = dim3(static_cast<unsigned>(mt), static_cast<unsigned>(nt),
+                         static_cast<unsigned>(splits));
+      int n = fits[vi][splits].load(std::memory_order_relaxed);
+      if (n == 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+          (void)cudaGetLastError();
+          n = -1;
+        }
+        fits[vi][splits].store(n == 0 ? -1 : n, std::memory_order_relaxed);
+      }
+      if (n >= mt * nt) break;
+    }
+    if (splits < 2) return -1;  // not worth it: the one-CTA-per-tile kernel
+    p.splits = splits;
+    if (cudaLaunchKernelEx(&cfg, kernel, xm, wm, p) != cudaSuccess) return PA_ERR_CUDA;
+    return launch_status();
+  };
+  static std::atomic<uint64_t> done[12];
   using N6 = QkvCfg<128, 6>;
   using W2 = QkvCfg<256, 2>;
+  if (!wide) {
+    int rs = -1;
+    if (bf && D == 64) rs = go_split(qkv_rope_append_kernel<__nv_bfloat16, 64, 128, 5, true>, &done[8], 0);
+    else if (bf) rs = go_split(qkv_rope_append_kernel<__nv_bfloat16, 128, 128, 5, true>, &done[9], 1);
+    else if (D == 64) rs = go_split(qkv_rope_append_kernel<__half, 64, 128, 5, true>, &done[10], 2);
+    else rs = go_split(qkv_rope_append_kernel<__half, 128, 128, 5, true>, &done[11], 3);
+    if (rs != -1) return rs;
+  }
   if (bf && D == 64)
-    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 64, 256, 2>, W2::kSmemBytes, &done[0])
-                : go(qkv_rope_append_kernel<__nv_bfloat16, 64, 128, 6>, N6::kSmemBytes, &done[1]);
+    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 64, 256, 2, false>, W2::kSmemBytes, &done[0])
+                : go(qkv_rope_append_kernel<__nv_bfloat16, 64, 128, 6, false>, N6::kSmemBytes, &done[1]);
   if (bf)
-    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 128, 256, 2>, W2::kSmemBytes, &done[2])
-                : go(qkv_rope_append_kernel<__nv_bfloat16, 128, 128, 6>, N6::kSmemBytes, &done[3]);
+    return wide ? go(qkv_rope_append_kernel<__nv_bfloat16, 128, 256, 2, false>, W2::kSmemBytes, &done[2])
+                : go(qkv_rope_append_kernel<__nv_bfloat16, 128, 128, 6, false>, N6::kSmemBytes, &done[3]);
   if (D == 64)
-    return wide ? go(qkv_rope_append_kernel<__half, 64, 256, 2>, W2::kSmemBytes, &done[4])
-                : go(qkv_rope_append_kernel<__half, 64, 128, 6>, N6::kSmemBytes, &done[5]);
-  return wide ? go(qkv_rope_append_kernel<__half, 128, 256, 2>, W2::kSmemBytes, &done[6])
-              : go(qkv_rope_append_kernel<__half, 128, 128, 6>, N6::kSmemBytes, &done[7]);
+    return wide ? go(qkv_rope_append_kernel<__half, 64, 256, 2, false>, W2::kSmemBytes, &done[4])
+                : go(qkv_rope_append_kernel<__half, 64, 128, 6, false>, N6::kSmemBytes, &done[5]);
+  return wide ? go(qkv_rope_append_kernel<__half, 128, 256, 2, false>, W2::kSmemBytes, &done[6])
+              : go(qkv_rope_append_kernel<__half, 128, 128, 6, false>, N6::kSmemBytes, &done[7]);
 }
 
 int pa_selftest_wait_timeout(int64_t limit_cycles, void* stream) {

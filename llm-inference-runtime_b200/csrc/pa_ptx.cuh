@@ -81,6 +81,72 @@ __device__ __forceinline__ bool mbar_wait_warp_limit(uint64_t* bar, uint32_t par
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, limit));
 }
 
+// ---------------------------------------------------------------- clusters
+// Rank of this CTA in its thread-block cluster.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of this CTA's shared-memory location `addr`
+// (a shared::cta address) in the CTA of rank `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f4(uint32_t addr, float x, float y, float z, float w) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x), "f"(y),
+               "f"(z), "f"(w)
+               : "memory");
+}
+// Arrival (release at cluster scope: orders this thread's earlier stores to
+// the other CTA) on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      "  .reg .pred p;\n"
+      "  mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "  selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait for a barrier that other CTAs of the cluster arrive on: bounded,
+// warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity) {
+  bool ok = mbar_try_wait_cluster(bar, parity);
+  if (!ok) {
+    const long long t0 = clock64();
+    while (!(ok = mbar_try_wait_cluster(bar, parity)))
+      if (clock64() - t0 > kWaitLimitCycles) break;
+  }
+  return __all_sync(0xffffffffu, ok);
+}
+__device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+// Split-phase cluster barrier: every thread of every CTA of the cluster
+// arrives once and waits once (warp-converged: .aligned).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // Tiled 4-D TMA load global -> shared, completion signalled on `bar` as
 // transaction bytes. No multicast: each CTA fetches its own tiles.

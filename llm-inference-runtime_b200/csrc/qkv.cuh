@@ -39,12 +39,17 @@ constexpr int kQkvThreads = 192;
 // loop runs (cos of pair i in column 128 + i, sin in 192 + i); with N=256
 // tiles TMEM is full, so they go to the released stage memory after it.
 // Either way the pair frequencies are computed once per CTA (smem).
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SPLITK = false>
 struct QkvCfg {
   static constexpr int kStageBytes = (kQkvBM + BN) * kQkvBK * 2;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + 512 + 1024;
+  // split-K: slots for the other splits' partial rows of the (at most two)
+  // row quarters this CTA finishes, 16 KB per quarter and source
+  static constexpr int kQuarterBytes = 32 * BN * 4;
+  static constexpr int kSlotBytes = SPLITK ? 4 * kQuarterBytes : 0;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kSlotBytes + 512 + 1024;
   static constexpr bool kTabTmem = BN == 128;
   static constexpr int kTmemCols = 256;
+  static_assert(!SPLITK || BN == 128, "split-K tiles are 128 columns");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -64,6 +69,7 @@ struct QkvParams {
   int64_t num_kv_indices;  // entries kv_indptr may index
   const int32_t* kv_indptr;
   int batch, page_size;
+  int splits;  // split-K: CTAs (one cluster) per output tile, 2..4; else 1
 };
 
 // Page slot of token m's row of kv head h, or -1 (padding row / error).
@@ -89,24 +95,34 @@ __device__ __forceinline__ int64_t qkv_slot(const QkvParams& p, int m, int h) {
   return page * p.page_stride + h * p.head_stride + (pos % p.page_size) * p.token_stride;
 }
 
-template <typename T, int D, int BN, int STAGES>
+template <typename T, int D, int BN, int STAGES, bool SPLITK>
 __global__ void __launch_bounds__(kQkvThreads, 2)
     qkv_rope_append_kernel(const __grid_constant__ CUtensorMap xmap,
                            const __grid_constant__ CUtensorMap wmap, const QkvParams p) {
+  using C = QkvCfg<BN, STAGES, SPLITK>;
   constexpr int S = STAGES;
-  constexpr int kStageBytes = QkvCfg<BN, STAGES>::kStageBytes;
-  constexpr bool kTabTmem = QkvCfg<BN, STAGES>::kTabTmem;
-  constexpr int kTmemCols = QkvCfg<BN, STAGES>::kTmemCols;
+  constexpr int kStageBytes = C::kStageBytes;
+  constexpr bool kTabTmem = C::kTabTmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+  uint8_t* slots = smem + S * kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(slots + C::kSlotBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
-  float* freq = reinterpret_cast<float*>(smem + S * kStageBytes + 256);  // [rotary_dim / 2]
+  uint64_t* red_full = acc_full + 1;  // [2], split-K: the other splits' rows landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 2);
+  float* freq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // [half]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kQkvBM, n0 = blockIdx.y * BN;
   const int nk = p.K / kQkvBK;
+  // Split-K: the `splits` CTAs of one cluster (grid z) each multiply the
+  // tile over a contiguous range of k blocks; row quarter q (TMEM lanes of
+  // warp q) is finished by the CTA of rank q % splits, which receives the
+  // other ranks' fp32 partial rows in its shared memory and adds all of
+  // them in rank order (deterministic).
+  const int nsplit = SPLITK ? p.splits : 1;
+  const int rank = SPLITK ? static_cast<int>(cluster_rank()) : 0;
+  const int kb0 = nk * rank / nsplit, kb1 = nk * (rank + 1) / nsplit;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&xmap);
@@ -116,24 +132,27 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
+    if (SPLITK)
+      for (int j = 0; j < 2; ++j) mbar_init(&red_full[j], (nsplit - 1) * 32);
     fence_mbar_init();
   }
   if (warp == 5) {
-    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_alloc(tmem_slot, C::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if constexpr (SPLITK) cluster_arrive();  // this CTA's barriers are initialised
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      for (int kb = 0; kb < nk; ++kb) {
-        const int st = kb % S;
-        if (kb >= S && !mbar_wait(&empty[st], ((kb / S) - 1) & 1)) {
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int it = kb - kb0, st = it % S;
+        if (it >= S && !mbar_wait(&empty[st], ((it / S) - 1) & 1)) {
           failed = true;
           break;
         }
@@ -144,15 +163,17 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
       }
       if (failed) set_status(PA_ERR_TIMEOUT);
     }
+    __syncwarp();
+    if constexpr (SPLITK) cluster_wait();
   } else if (warp == 5) {
     // ------------------------------------------------------------ tcgen05 issuer
     if (lane == 0) {
       const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       const uint32_t idesc = umma_idesc_f16(ab, kQkvBM, BN, 0);
       const uint32_t base = smem_u32(smem);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int st = kb % S;
-        if (!mbar_wait(&full[st], (kb / S) & 1)) {
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int it = kb - kb0, st = it % S;
+        if (!mbar_wait(&full[st], (it / S) & 1)) {
           failed = true;
           break;
         }
@@ -161,7 +182,7 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
 #pragma unroll
         for (int kk = 0; kk < kQkvBK / 16; ++kk)
           umma_f16(tmem, umma_desc_sw128(sa + kk * 32, 16, 1024),
-                   umma_desc_sw128(sb + kk * 32, 16, 1024), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                   umma_desc_sw128(sb + kk * 32, 16, 1024), idesc, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&empty[st]);
       }
       // on a timeout the accumulator is garbage; the epilogue still runs
@@ -169,6 +190,8 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
       umma_commit(acc_full);
       if (failed) set_status(PA_ERR_TIMEOUT);
     }
+    __syncwarp();
+    if constexpr (SPLITK) cluster_wait();
   } else {
     // ------------------------------------------------------------ epilogue
     const int r = warp * 32 + lane;  // tile row == TMEM lane
@@ -181,12 +204,14 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
                                                            : (n0 - qcols - kcols) / D);
     const bool active = m < p.M;
     const int half = p.rotary_dim / 2;
+    const int owner = warp % nsplit, jq = warp / nsplit;  // this quarter's finisher
+    const bool mine = owner == rank;
     // Page slots of this row's k / v heads, looked up (three dependent
     // global loads) while the main loop runs.
     int64_t slot[HPT];
 #pragma unroll
     for (int hh = 0; hh < HPT; ++hh)
-      slot[hh] = (active && region > 0) ? qkv_slot(p, m, head0 + hh) : -1;
+      slot[hh] = (mine && active && region > 0) ? qkv_slot(p, m, head0 + hh) : -1;
     const int pos = active ? __ldg(p.positions + m) : 0;
     if (threadIdx.x < half) freq[threadIdx.x] = rope_freq(threadIdx.x, p.rotary_dim, p.inv_scale,
                                                           p.log2_theta);
@@ -229,18 +254,48 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
         }
       }
     };
+    // split-K slot of (this quarter, source rank z) in the finishing CTA:
+    // row `lane` at 4 * BN bytes, 16-byte chunk c at (c & ~7) | ((c ^ lane) & 7)
+    auto slot_row = [&](int z) {
+      return smem_u32(slots) + (jq * (nsplit - 1) + (z < owner ? z : z - 1)) * C::kQuarterBytes +
+             lane * (BN * 4);
+    };
+    auto chunk_off = [&](int c) { return ((c & ~7) | ((c ^ lane) & 7)) * 16; };
     if constexpr (kTabTmem) {
-      if (region < 2) {
+      if (mine && region < 2) {
 #pragma unroll 1
         for (int i0 = 0; i0 < half; i0 += 16) tabulate(i0);
         tmem_wait_st();
       }
     }
     const bool ok = mbar_wait_warp(acc_full, 0);
-    if (!ok) {
-      if (lane == 0) set_status(PA_ERR_TIMEOUT);
-    } else {
-      tc_fence_after();
+    if (!ok && lane == 0) set_status(PA_ERR_TIMEOUT);
+    tc_fence_after();
+    bool go = ok;
+    if constexpr (SPLITK) {
+      cluster_wait();  // every CTA of the cluster has initialised its barriers
+      if (!mine) {
+        // push this quarter's partial rows to the finishing CTA (also after
+        // a timeout, so that it does not wait for them in vain)
+        const uint32_t dst = cluster_map(slot_row(rank), owner);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(taddr + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            st_cluster_f4(dst + chunk_off(c * 8 + e), v[4 * e], v[4 * e + 1], v[4 * e + 2],
+                          v[4 * e + 3]);
+        }
+        mbar_arrive_remote(cluster_map(smem_u32(&red_full[jq]), owner));
+        go = false;
+      } else if (!mbar_wait_cluster_warp(&red_full[jq], 0)) {
+        if (lane == 0) set_status(PA_ERR_TIMEOUT);
+        go = false;
+      }
+    }
+    if (go) {
       if constexpr (!kTabTmem) {
         // in the stage memory the main loop has released: column r of
         // [2 * half][128] floats, read back only by this thread
@@ -253,9 +308,36 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
       for (int hh = 0; hh < HPT; ++hh) {
         float a[D];
         __syncwarp();
+        if constexpr (SPLITK) {
+          // the splits' partial rows, added in rank order
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) tmem_ld32(taddr + hh * D + c * 32, a + c * 32);
-        tmem_wait_ld();
+          for (int c = 0; c < D / 32; ++c) {
+#pragma unroll 1
+            for (int z = 0; z < nsplit; ++z) {
+              float v[32];
+              if (z == rank) {
+                tmem_ld32(taddr + hh * D + c * 32, v);
+                tmem_wait_ld();
+              } else {
+                const uint32_t src = slot_row(z);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float4 f = ld_shared_f4(src + chunk_off((hh * D + c * 32) / 4 + e));
+                  v[4 * e] = f.x;
+                  v[4 * e + 1] = f.y;
+                  v[4 * e + 2] = f.z;
+                  v[4 * e + 3] = f.w;
+                }
+              }
+#pragma unroll
+              for (int e = 0; e < 32; ++e) a[c * 32 + e] = z == 0 ? v[e] : a[c * 32 + e] + v[e];
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) tmem_ld32(taddr + hh * D + c * 32, a + c * 32);
+          tmem_wait_ld();
+        }
         if (region < 2) {
           // fp32 rotation of the accumulator (rope_rotate, as rope_kernel),
           // 16 pairs per table read; padding rows too (nothing stores them),
@@ -326,7 +408,7 @@ __global__ void __launch_bounds__(kQkvThreads, 2)
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, C::kTmemCols);
   }
 }
 

@@ -122,3 +122,21 @@ def test_fused_qkv_fp16_and_partial_rotary(fused):
 def test_fused_qkv_rejects_unsupported(fused):
     w = torch.zeros(100, 2048, dtype=torch.bfloat16, device=DEV)
     assert not fused.supported(w, 32, 4, 64, torch.bfloat16)
+
+
+@pytest.mark.parametrize("geom", [(2048, 32, 4, 64), (4096, 32, 8, 128)])
+def test_fused_qkv_split_k_is_deterministic(fused, geom):
+    # decode-sized batches split K over a cluster of CTAs; the partial tiles
+    # are added in a fixed order, so repeated calls agree bit for bit
+    hidden, hq, hkv, d = geom
+    rng = np.random.default_rng(5)
+    c = _case(rng, 37, hidden, hq, hkv, d, "HND", torch.bfloat16)
+    outs = []
+    for _ in range(3):
+        pool = c["pool"].to(DEV)
+        q = fused.qkv_rope_append(c["x"].to(DEV), c["w"].to(DEV), hq, _t(c["bi"]), _t(c["pos"]),
+                                  pool, _t(c["indices"]), _t(c["indptr"]))
+        outs.append((q.cpu(), pool.cpu()))
+    for q, pool in outs[1:]:
+        assert torch.equal(q, outs[0][0])
+        assert torch.equal(pool, outs[0][1])
