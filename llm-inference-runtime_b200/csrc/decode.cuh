@@ -387,6 +387,8 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
   StreamCursor cc = pc;
   const int panel_bytes = HB * 2048;
 
+  // K/V pages are read once per launch: first to leave L2.
+  const uint64_t evict_first = l2_evict_first_policy();
   // Fills stage `stage` with page `page` of head block `hblk` (one thread).
   auto issue = [&](int stage, int page, int hblk) {
     if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
@@ -399,8 +401,10 @@ __global__ void __launch_bounds__(decode_cta_warps(D) * 32, 1)
     const int c1 = p.heads_inner ? h0 : 0, c2 = p.heads_inner ? 0 : h0;
 #pragma unroll
     for (int pn = 0; pn < PANELS; ++pn) {
-      tma_load_4d(dst + pn * panel_bytes, &kmap, &bars[stage], pn * 64, c1, c2, page);
-      tma_load_4d(dst + (PANELS + pn) * panel_bytes, &vmap, &bars[stage], pn * 64, c1, c2, page);
+      tma_load_4d_hint(dst + pn * panel_bytes, &kmap, &bars[stage], pn * 64, c1, c2, page,
+                       evict_first);
+      tma_load_4d_hint(dst + (PANELS + pn) * panel_bytes, &vmap, &bars[stage], pn * 64, c1, c2,
+                       page, evict_first);
     }
   };
 
