@@ -244,7 +244,9 @@ int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorM
   constexpr int smem = PfCfg<D>::kSmemBytes;
   if (allow_smem(prefill_kernel<T, D>, smem, &done, dev) != cudaSuccess) return PA_ERR_CUDA;
   if (grid <= 0) return PA_OK;
-  if (grid > 0x7fffffffLL) return PA_ERR_INVALID_ARGUMENT;
+  // persistent: one CTA per SM at most, each taking items until none is left
+  const int sms = sm_count(dev) > 0 ? sm_count(dev) : 148;
+  grid = std::min<int64_t>(grid, sms);
   prefill_kernel<T, D><<<static_cast<unsigned>(grid), kPfThreads, smem, stream>>>(qm, km, vm, prm);
   return launch_status();
 }
@@ -991,6 +993,7 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.hdr = reinterpret_cast<const PrefillPlanHeader*>(ws + L.hdr);
   p.items = reinterpret_cast<const int4*>(ws + L.items);
+  p.sched = reinterpret_cast<int32_t*>(ws + L.hdr + offsetof(PrefillPlanHeader, next_item));
   p.q_rows = nullptr;
   const int dev = current_device();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1145,6 +1148,8 @@ int cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_
   p.scale_log2 = scale * 1.4426950408889634f;
   p.hdr = reinterpret_cast<const PrefillPlanHeader*>(ws + L.prefill + PL.hdr);
   p.items = reinterpret_cast<const int4*>(ws + L.prefill + PL.items);
+  p.sched = reinterpret_cast<int32_t*>(ws + L.prefill + PL.hdr +
+                                       offsetof(PrefillPlanHeader, next_item));
   p.q_rows = reinterpret_cast<const int32_t*>(ws + L.q_rows);
   const bool bf16 = cache->dtype == PA_DTYPE_BF16;
   st = bf16 ? (D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, p, L.prefill_items, dev, s)

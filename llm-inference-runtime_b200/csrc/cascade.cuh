@@ -138,6 +138,8 @@ __global__ void cascade_plan_kernel(const int32_t* __restrict__ shared_indptr,
     ph->num_qo_heads = hq;
     ph->head_dim = head_dim;
     ph->queries_per_tile = span;
+    ph->next_item = 0;
+    ph->ctas_done = 0;
     ph->magic = kPrefillMagic;
     ch->status = bad ? PA_ERR_DEVICE_CHECK : PA_OK;
     ch->num_chunks = nch;

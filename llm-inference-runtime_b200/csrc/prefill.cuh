@@ -56,8 +56,9 @@ constexpr int kPfKeys = 128;  // keys per K/V tile (MMA N of S, K of PV): 8 page
 // Warpgroup 2: warp 8 TMA producer, warp 9 tcgen05 issuer, warps 10 / 11
 // relay K / V TMA completions to the issuer.
 // Launched at 168 registers per thread (384 x 168 = 64512 of 65536); after
-// setup warpgroup 2 drops to 56 and warpgroups 0-1 rise to 224:
-// 2 x 128 x 224 + 128 x 56 = 64512, exactly the launch total.
+// setup warpgroup 2 rises to 88 and warpgroups 0-1 to 208:
+// 2 x 128 x 208 + 128 x 88 = 64512, exactly the launch total (the producer
+// and the issuer carry the persistent loop's item state; at 56 they spilled).
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfProducerWarp = 8;
 constexpr int kPfMmaWarp = 9;
@@ -71,8 +72,9 @@ constexpr int kPfBarV = 4;
 constexpr int kPfBarPThreads = 128 + 32;
 constexpr int kPfBarKVThreads = 32 + 32;
 constexpr int kPfThreads = 384;
-constexpr uint32_t kPfRegsSoftmax = 224;
-constexpr uint32_t kPfRegsOther = 56;
+constexpr int kPfItemReaders = 11;  // warps reading each work-item slot: 8 softmax, issuer, 2 relays
+constexpr uint32_t kPfRegsSoftmax = 208;
+constexpr uint32_t kPfRegsOther = 88;
 static_assert(2 * 128 * kPfRegsSoftmax + 128 * kPfRegsOther <= kPfThreads * 168,
               "register split must fit the launch allocation");
 static_assert(kPfRegsSoftmax % 8 == 0 && kPfRegsOther % 8 == 0 && kPfRegsOther >= 24,
@@ -88,7 +90,9 @@ struct PrefillPlanHeader {
   int32_t num_qo_heads;
   int32_t head_dim;
   int32_t queries_per_tile;
-  int32_t reserved[8];
+  int32_t next_item;  // work-item counter of the persistent kernel (zero between launches)
+  int32_t ctas_done;  // CTAs that have stopped taking items
+  int32_t reserved[6];
 };
 
 struct PrefillWsLayout {
@@ -120,9 +124,12 @@ struct PfCfg {
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
   static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-  // barriers: q_full, s_full[2], o_done[2], mma_done, k_full/k_empty/v_full/v_empty[S]
-  static constexpr int kNumBars = 6 + 4 * kStages;
-  static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+  // barriers: q_full, s_full[2], o_done[2], mma_done, k_full/k_empty/v_full/v_empty[S],
+  // item_full[3], item_empty[3], q_empty
+  static constexpr int kNumBars = 6 + 4 * kStages + 7;
+  static constexpr int kOffSlots = kOffBar + kNumBars * 8 + 16;  // three work-item slots
+  static constexpr int kSmemBytes = kOffSlots + 3 * 64 + 1024;
+  static_assert(kOffSlots % 8 == 0, "shared-memory alignment");
   // TMEM columns: S0 | S1 | O0 | O1 (P_t is written over the first half of S_t)
   static constexpr uint32_t kTmemCols = 512;
 };
@@ -140,6 +147,7 @@ struct PrefillParams {
   float scale_log2;
   const PrefillPlanHeader* hdr;
   const int4* items;
+  int32_t* sched;  // the header's next_item, ctas_done
   // Optional: first q row of request b (default qo_indptr[b]). Lets several
   // requests read the same queries while writing their own output rows —
   // the key chunks of a shared prefix (cascade decode).
@@ -236,12 +244,52 @@ __global__ void prefill_plan_kernel(const int32_t* __restrict__ qo_indptr,
     hdr->num_qo_heads = hq;
     hdr->head_dim = head_dim;
     hdr->queries_per_tile = qt;
+    hdr->next_item = 0;
+    hdr->ctas_done = 0;
     hdr->magic = kPrefillMagic;
     if (err) set_status(PA_ERR_DEVICE_CHECK);
   }
 }
 
 // ---------------------------------------------------------------------- run
+// Persistent: one CTA per SM takes work items from the plan's list (longest
+// first) through the counter in the plan header. The producer claims one
+// item ahead and publishes it (its geometry worked out) in a two-slot ring
+// that every other warp reads, so the next item's Q tiles and first K / V
+// tiles load while the current item's last steps run, the issuer starts the
+// next item's S MMAs right after the current item's last PV (while the
+// softmax warps store O), and no CTA launch sits between items. Barrier
+// phases run on across items: K / V ring stages by the CTA's running tile
+// count, S / O hand-offs by its running step count, Q by its item count.
+
+// One item's geometry, as every warp of the CTA needs it.
+struct PfItem {
+  int b, h, t0, qo_start, qo_len, q_row0, page0, npages, kv_len, ntiles;  // ntiles < 0: stop
+};
+
+__device__ __forceinline__ PfItem pf_item(const PrefillParams& p, int idx) {
+  PfItem w;
+  if (idx < 0) {
+    w = PfItem{0, 0, 0, 0, 0, 0, 0, 0, 0, -1};
+    return w;
+  }
+  const int4 it = p.items[idx];
+  w.b = it.x;
+  w.h = it.y;
+  w.t0 = it.z;
+  w.qo_start = __ldg(p.qo_indptr + w.b);
+  w.qo_len = __ldg(p.qo_indptr + w.b + 1) - w.qo_start;
+  w.q_row0 = p.q_rows != nullptr ? __ldg(p.q_rows + w.b) : w.qo_start;
+  w.page0 = __ldg(p.kv_indptr + w.b);
+  w.npages = __ldg(p.kv_indptr + w.b + 1) - w.page0;
+  w.kv_len = w.npages > 0 ? (w.npages - 1) * kPage + __ldg(p.kv_last_page_len + w.b) : 0;
+  // keys this item can see: up to its last query's position (causal) or all
+  const int q_hi = min(w.t0 + 2 * p.qt, w.qo_len);
+  const int kv_end = p.causal ? min(w.kv_len, w.kv_len - w.qo_len + q_hi) : w.kv_len;
+  w.ntiles = kv_end > 0 ? (kv_end + kPfKeys - 1) / kPfKeys : 0;
+  return w;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -257,12 +305,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* s_full = bars + 1;  // [2] per Q tile
   uint64_t* o_done = bars + 3;    // [2]
-  uint64_t* mma_done = bars + 5;  // every MMA of the item has completed
+  uint64_t* mma_done = bars + 5;  // every MMA of the CTA has completed
   uint64_t* k_full = bars + 6;
   uint64_t* k_empty = k_full + S;
   uint64_t* v_full = k_empty + S;
   uint64_t* v_empty = v_full + S;
+  uint64_t* item_full = v_empty + S;   // [3] item slot published
+  uint64_t* item_empty = item_full + 3;  // [3] every reader is done with it
+  uint64_t* q_empty = item_empty + 3;    // the item's S MMAs are done with the Q tiles
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+  PfItem* slots = reinterpret_cast<PfItem*>(smem + C::kOffSlots);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const PrefillPlanHeader* hdr = p.hdr;
@@ -272,21 +324,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (blockIdx.x == 0 && threadIdx.x == 0) set_status(PA_ERR_NOT_PLANNED);
     return;
   }
-  if (hdr->status != PA_OK || static_cast<int>(blockIdx.x) >= hdr->num_items) return;
-
-  const int4 item = p.items[blockIdx.x];
-  const int b = item.x, h = item.y, t0 = item.z;
+  if (hdr->status != PA_OK) return;
+  const int num_items = hdr->num_items;
   const int G = p.group, QT = p.qt, hq = p.num_qo_heads;
-  const int qo_start = __ldg(p.qo_indptr + b);
-  const int qo_len = __ldg(p.qo_indptr + b + 1) - qo_start;
-  const int q_row0 = p.q_rows != nullptr ? __ldg(p.q_rows + b) : qo_start;
-  const int page0 = __ldg(p.kv_indptr + b);
-  const int npages = __ldg(p.kv_indptr + b + 1) - page0;
-  const int kv_len = npages > 0 ? (npages - 1) * kPage + __ldg(p.kv_last_page_len + b) : 0;
-  // keys this item can see: up to its last query's position (causal) or all
-  const int q_hi = min(t0 + 2 * QT, qo_len);
-  const int kv_end = p.causal ? min(kv_len, kv_len - qo_len + q_hi) : kv_len;
-  const int ntiles = kv_end > 0 ? (kv_end + kPfKeys - 1) / kPfKeys : 0;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&qmap);
@@ -297,6 +337,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&o_done[t], 1);
     }
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], kPfItemReaders);
+    }
     for (int s = 0; s < S; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -304,6 +348,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&v_empty[s], 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(q_empty, 1);
     fence_mbar_init();
   }
   if (warp == kPfMmaWarp) {
@@ -315,102 +360,177 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
+
+  // Work items travel in a three-slot ring: item i in slot i % 3. Readers
+  // wait for their item's slot and release it when they are done with the
+  // item (the softmax warps after storing O, so they can read the item's
+  // fields again there); the producer writes item i + 3 over it.
+  auto wait_item = [&](int it) {
+    PfItem w;
+    if (!mbar_wait_warp(&item_full[it % 3], (it / 3) & 1)) {
+      failed = true;
+      w = PfItem{0, 0, 0, 0, 0, 0, 0, 0, 0, -1};
+    } else {
+      w = slots[it % 3];
+    }
+    return w;
+  };
+  auto done_item = [&](int it) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&item_empty[it % 3]);
+  };
+  auto next_item = [&](int it) {
+    const PfItem w = wait_item(it);
+    done_item(it);
+    return w;
+  };
+
   if (warp == kPfProducerWarp) {
     regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ producer
-    const int c1 = p.heads_inner ? h : 0, c2 = p.heads_inner ? 0 : h;
-    if (lane == 0 && ntiles > 0) {
-      mbar_arrive_expect_tx(q_full, 2 * C::kQBytes);
-#pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_3d(sQ + t * C::kQBytes + pn * C::kPanelBytes, &qmap, q_full, pn * 64, h * G,
-                      q_row0 + t0 + t * QT);
-    }
-    for (int j = 0; j < ntiles && !failed; ++j) {
-      const int st = j % S, use = j / S;
-      const int np = min(8, npages - 8 * j);
-      int page = 0;
-      if (lane < np) {
-        page = __ldg(p.kv_indices + page0 + 8 * j + lane);
-        if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
-          set_status(PA_ERR_DEVICE_CHECK);
-          page = 0;
-        }
+    auto claim = [&]() {
+      int i = -1;
+      if (lane == 0 && !failed) {
+        i = atomicAdd(&p.sched[0], 1);
+        if (i >= num_items) i = -1;
       }
-      const uint32_t bytes = static_cast<uint32_t>(np) * C::kPanels * 2048;
-      if (use > 0 && !mbar_wait_warp(&k_empty[st], (use - 1) & 1)) failed = true;
-      if (!failed) {
-        if (lane == 0) mbar_arrive_expect_tx(&k_full[st], bytes);
-        __syncwarp();
-        if (lane < np) {
-#pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_4d(sK + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &kmap,
-                        &k_full[st], pn * 64, c1, c2, page);
-        }
-      }
-      if (!failed && use > 0 && !mbar_wait_warp(&v_empty[st], (use - 1) & 1)) failed = true;
-      if (!failed) {
-        if (lane == 0) mbar_arrive_expect_tx(&v_full[st], bytes);
-        __syncwarp();
-        if (lane < np) {
-#pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_4d(sV + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &vmap,
-                        &v_full[st], pn * 64, c1, c2, page);
-        }
+      return __shfl_sync(0xffffffffu, i, 0);
+    };
+    auto publish = [&](int slot, const PfItem& w) {
+      if (lane == 0) {
+        slots[slot] = w;
+        mbar_arrive(&item_full[slot]);  // release: the slot's contents first
       }
       __syncwarp();
+    };
+    PfItem w = pf_item(p, claim());
+    publish(0, w);
+    uint32_t kt = 0;  // K / V tiles loaded so far: ring position
+    int qc = 0;       // items whose Q tiles were loaded
+    for (int it = 0; w.ntiles >= 0; ++it) {
+      // claim and publish item it + 1; its slot was item it - 2's
+      const int nxt = claim();
+      if (it >= 2 && !mbar_wait_warp(&item_empty[(it + 1) % 3], ((it - 2) / 3) & 1))
+        failed = true;
+      const PfItem wn = pf_item(p, failed ? -1 : nxt);
+      publish((it + 1) % 3, wn);
+      if (w.ntiles > 0) {
+        const int c1 = p.heads_inner ? w.h : 0, c2 = p.heads_inner ? 0 : w.h;
+        // Q tiles, once the previous item's S MMAs are done with the buffer
+        if (qc > 0 && !mbar_wait_warp(q_empty, (qc - 1) & 1)) failed = true;
+        ++qc;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(q_full, 2 * C::kQBytes);
+#pragma unroll
+          for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int pn = 0; pn < C::kPanels; ++pn)
+              tma_load_3d(sQ + t * C::kQBytes + pn * C::kPanelBytes, &qmap, q_full, pn * 64,
+                          w.h * G, w.q_row0 + w.t0 + t * QT);
+        }
+        for (int j = 0; j < w.ntiles; ++j) {
+          const uint32_t g = kt + j;
+          const int st = g % S, use = g / S;
+          const int np = min(8, w.npages - 8 * j);
+          int page = 0;
+          if (lane < np) {
+            page = __ldg(p.kv_indices + w.page0 + 8 * j + lane);
+            if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
+              set_status(PA_ERR_DEVICE_CHECK);
+              page = 0;
+            }
+          }
+          const uint32_t bytes = static_cast<uint32_t>(np) * C::kPanels * 2048;
+          // after a timeout the stages still complete (no bytes expected), so
+          // the relays and the issuer keep their rounds without waiting long
+          if (use > 0 && !failed && !mbar_wait_warp(&k_empty[st], (use - 1) & 1)) failed = true;
+          if (lane == 0) mbar_arrive_expect_tx(&k_full[st], failed ? 0u : bytes);
+          __syncwarp();
+          if (lane < np && !failed) {
+#pragma unroll
+            for (int pn = 0; pn < C::kPanels; ++pn)
+              tma_load_4d(sK + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &kmap,
+                          &k_full[st], pn * 64, c1, c2, page);
+          }
+          if (use > 0 && !failed && !mbar_wait_warp(&v_empty[st], (use - 1) & 1)) failed = true;
+          if (lane == 0) mbar_arrive_expect_tx(&v_full[st], failed ? 0u : bytes);
+          __syncwarp();
+          if (lane < np && !failed) {
+#pragma unroll
+            for (int pn = 0; pn < C::kPanels; ++pn)
+              tma_load_4d(sV + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &vmap,
+                          &v_full[st], pn * 64, c1, c2, page);
+          }
+          __syncwarp();
+        }
+        kt += w.ntiles;
+      }
+      w = wn;
     }
-    if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
+    if (lane == 0) {
+      if (failed) set_status(PA_ERR_TIMEOUT);
+      // the last CTA to stop claiming resets the counter for the next launch
+      __threadfence();
+      if (atomicAdd(&p.sched[1], 1) == static_cast<int>(gridDim.x) - 1) {
+        atomicExch(&p.sched[0], 0);
+        atomicExch(&p.sched[1], 0);
+      }
+    }
   } else if (warp == kPfMmaWarp) {
     regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ tcgen05 issuer
     // The whole warp runs this loop and takes part in the named barriers
     // (hand-offs: P_t from softmax warpgroup t, K / V tiles from the relay
-    // warp); lane 0 issues the MMAs. The issuing thread touches no shared
+    // warps); lane 0 issues the MMAs. The issuing thread touches no shared
     // memory between MMAs: with only a couple of MMAs queued, a
     // shared-memory wait on this thread would idle the tensor pipe.
-    if (ntiles > 0) {
-      const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      const uint32_t idesc_s = umma_idesc_f16(ab, kPfRows, kPfKeys, 0);
-      const uint32_t idesc_o = umma_idesc_f16(ab, kPfRows, D, 1);
-      // Shared-memory descriptors are formed once: a descriptor's address
-      // field is the byte address / 16 (all of shared memory fits its 14
-      // bits), so stepping through an operand is one add of a constant.
-      // Between hand-offs the issuing thread then runs little more than the
-      // MMAs themselves: it shares its sub-partition's issue slots with two
-      // softmax warps, and every slot it waits for leaves the tensor pipe's
-      // short queue emptier.
-      const uint64_t dq0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
-      const uint64_t dk0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
-      const uint64_t dv0 = umma_desc_sw128(smem_u32(sV), C::kPanelBytes, 1024);
-      constexpr uint64_t kQStep = C::kQBytes >> 4, kTileStep = C::kTileBytes >> 4;
-      if (!mbar_wait_warp(q_full, 0)) failed = true;
-      // S_t = Q_t K_j^T into TMEM columns [128 t, 128 t + 128); lane 0 only
-      auto issue_s = [&](int t, int j) {
-        const uint64_t dq = dq0 + t * kQStep, dk = dk0 + (j % S) * kTileStep;
-        const uint32_t d = tmem + t * kPfKeys;
+    const int ab = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+    const uint32_t idesc_s = umma_idesc_f16(ab, kPfRows, kPfKeys, 0);
+    const uint32_t idesc_o = umma_idesc_f16(ab, kPfRows, D, 1);
+    // Shared-memory descriptors are formed once: a descriptor's address
+    // field is the byte address / 16 (all of shared memory fits its 14
+    // bits), so stepping through an operand is one add of a constant.
+    // Between hand-offs the issuing thread then runs little more than the
+    // MMAs themselves: it shares its sub-partition's issue slots with two
+    // softmax warps, and every slot it waits for leaves the tensor pipe's
+    // short queue emptier.
+    const uint64_t dq0 = umma_desc_sw128(smem_u32(sQ), 16, 1024);
+    const uint64_t dk0 = umma_desc_sw128(smem_u32(sK), 16, 1024);
+    const uint64_t dv0 = umma_desc_sw128(smem_u32(sV), C::kPanelBytes, 1024);
+    constexpr uint64_t kQStep = C::kQBytes >> 4, kTileStep = C::kTileBytes >> 4;
+    // S_t = Q_t K_g^T (g: the CTA's running tile count) into TMEM columns
+    // [128 t, 128 t + 128); lane 0 only
+    auto issue_s = [&](int t, uint32_t g) {
+      const uint64_t dq = dq0 + t * kQStep, dk = dk0 + (g % S) * kTileStep;
+      const uint32_t d = tmem + t * kPfKeys;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = ((kk >> 2) * C::kPanelBytes + (kk & 3) * 32) >> 4;
-          umma_f16(d, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-        if (t == 1) umma_commit(&k_empty[j % S]);
-      };
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = ((kk >> 2) * C::kPanelBytes + (kk & 3) * 32) >> 4;
+        umma_f16(d, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(&s_full[t]);
+      if (t == 1) umma_commit(&k_empty[g % S]);
+    };
+    uint32_t kt = 0;
+    int qc = 0;
+    for (int it = 0;; ++it) {
+      const PfItem w = next_item(it);
+      if (w.ntiles < 0) break;
+      if (w.ntiles == 0) continue;
+      const int ntiles = w.ntiles;
+      if (!mbar_wait_warp(q_full, qc & 1)) failed = true;
+      ++qc;
       named_bar_sync(kPfBarK, kPfBarKVThreads);
       if (lane == 0) {
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
+        issue_s(0, kt);
+        issue_s(1, kt);
+        if (ntiles == 1) umma_commit(q_empty);
       }
       __syncwarp();
       for (int j = 0; j < ntiles; ++j) {
-        const int st = j % S;
-        const uint64_t dv = dv0 + st * kTileStep;
+        const uint32_t g = kt + j;
+        const uint64_t dv = dv0 + (g % S) * kTileStep;
         named_bar_sync(kPfBarV, kPfBarKVThreads);
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
@@ -433,19 +553,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                   : "memory");
             }
             umma_commit(&o_done[t]);
-            if (t == 1) umma_commit(&v_empty[st]);
+            if (t == 1) umma_commit(&v_empty[g % S]);
             // the next S_t overwrites P_t only after this PV (same thread, in order)
-            if (j + 1 < ntiles) issue_s(t, j + 1);
+            if (j + 1 < ntiles) {
+              issue_s(t, g + 1);
+              if (t == 1 && j + 2 == ntiles) umma_commit(q_empty);  // the item's last S
+            }
           }
           __syncwarp();
         }
       }
-      // every MMA done before the TMEM is released
-      if (lane == 0) umma_commit(mma_done);
-      __syncwarp();
-      if (!mbar_wait_warp(mma_done, 0)) failed = true;
-      if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
+      kt += ntiles;
     }
+    // every MMA done before the TMEM is released
+    if (lane == 0) umma_commit(mma_done);
+    __syncwarp();
+    if (!mbar_wait_warp(mma_done, 0)) failed = true;
+    if (failed && lane == 0) set_status(PA_ERR_TIMEOUT);
   } else if (warp == kPfRelayWarp || warp == kPfRelayVWarp) {
     regs_dec<kPfRegsOther>();
     // ------------------------------------------------------------ relays
@@ -458,31 +582,50 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t* full = is_k ? k_full : v_full;
     const int bar = is_k ? kPfBarK : kPfBarV;
     bool rfail = false;
-    for (int j = 0; j < ntiles; ++j) {
-      if (!rfail && !mbar_wait_warp(&full[j % S], (j / S) & 1)) rfail = true;
-      named_bar_sync(bar, kPfBarKVThreads);
+    uint32_t kt = 0;
+    for (int it = 0;; ++it) {
+      const PfItem w = next_item(it);
+      if (w.ntiles < 0) break;
+      for (int j = 0; j < w.ntiles; ++j) {
+        const uint32_t g = kt + j;
+        if (!rfail && !mbar_wait_warp(&full[g % S], (g / S) & 1)) rfail = true;
+        named_bar_sync(bar, kPfBarKVThreads);
+      }
+      kt += w.ntiles;
     }
-    if (rfail && lane == 0) set_status(PA_ERR_TIMEOUT);
+    if ((rfail || failed) && lane == 0) set_status(PA_ERR_TIMEOUT);
   } else {
     regs_inc<kPfRegsSoftmax>();
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;                 // Q tile
     const int r = (warp & 3) * 32 + lane;    // tile row == TMEM lane
     const int qi = t * QT + r / G, gi = r % G;
-    const bool row_ok = r / G < QT && t0 + qi < qo_len;
-    const int qpos = kv_len - qo_len + t0 + qi;
-    const int lim = p.causal ? min(qpos + 1, kv_len) : kv_len;
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_addr + t * kPfKeys;
     const uint32_t tO = tmem + lane_addr + 256 + t * D;
+    uint32_t kt = 0;  // running tile count = running step count
+    for (int it = 0;; ++it) {
+    int ntiles, kv_len, lim;
+    {
+      const PfItem w = wait_item(it);
+      ntiles = w.ntiles;
+      kv_len = w.kv_len;
+      const int qpos = kv_len - w.qo_len + w.t0 + qi;
+      lim = p.causal ? min(qpos + 1, kv_len) : kv_len;
+    }
+    if (ntiles < 0) {
+      done_item(it);
+      break;
+    }
     float m_used = -INFINITY, l = 0.f;
     float s[kPfKeys];
     // Every step ends with this warpgroup meeting the issuer on the P_t
     // barrier, also after a timeout (the work is skipped then), so every
     // named barrier of the item completes.
     for (int j = 0; j < ntiles; ++j) {
+      const uint32_t g = kt + j;
       if (!failed) do {
-      if (!mbar_wait_warp(&s_full[t], j & 1)) {
+      if (!mbar_wait_warp(&s_full[t], g & 1)) {
         failed = true;
         break;
       }
@@ -525,7 +668,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       // Rows whose max moved rescale O_t (after PV_t of the previous tile).
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        if (!mbar_wait_warp(&o_done[t], (j - 1) & 1)) {
+        if (!mbar_wait_warp(&o_done[t], (g - 1) & 1)) {
           failed = true;
           break;
         }
@@ -548,8 +691,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // loaded): tile 0's warpgroup zeroes those V rows before its PV, which
       // precedes tile 1's PV on the tensor pipe.
       if (t == 0 && j == ntiles - 1 && key0 + kPfKeys > kv_len) {
-        const int st = j % S;
-        if (!mbar_wait_warp(&v_full[st], (j / S) & 1)) {
+        const int st = g % S;
+        if (!mbar_wait_warp(&v_full[st], (g / S) & 1)) {
           failed = true;
           break;
         }
@@ -570,42 +713,49 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       // the next scores come after this PV).
       named_bar_sync(kPfBarP + t, kPfBarPThreads);
     }
-    // ---- epilogue: O_t / l -> out, LSE
+    // ---- epilogue: O_t / l -> out, LSE (the issuer is already running the
+    // next item's first S MMAs; its first PV waits for this warpgroup's next
+    // P_t hand-off, so O_t is not overwritten before it is read here)
     if (!failed && ntiles > 0) {
-      if (!mbar_wait_warp(&o_done[t], (ntiles - 1) & 1)) failed = true;
+      if (!mbar_wait_warp(&o_done[t], (kt + ntiles - 1) & 1)) failed = true;
     }
     if (failed) {
       set_status(PA_ERR_TIMEOUT);
     } else {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) +
-                (static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi) * D;
+      const PfItem& w = slots[it % 3];  // still this item's: released below
+      const bool row_ok = r / G < QT && w.t0 + qi < w.qo_len;
+      const size_t row = static_cast<size_t>(w.qo_start + w.t0 + qi) * hq + w.h * G + gi;
+      T* orow = reinterpret_cast<T*>(p.out) + row * D;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        if (ntiles > 0) {
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-        } else {
+      // all of the row's O columns in one TMEM round trip (the scores'
+      // registers are free here)
+      float o[D];
+      if (ntiles > 0) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0.f;
-        }
-        if (row_ok) {
+        for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, o + c * 32);
+        tmem_wait_ld();
+      } else {
 #pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 w;
-            w.x = pack2<T>(o[e] * inv, o[e + 1] * inv);
-            w.y = pack2<T>(o[e + 2] * inv, o[e + 3] * inv);
-            w.z = pack2<T>(o[e + 4] * inv, o[e + 5] * inv);
-            w.w = pack2<T>(o[e + 6] * inv, o[e + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = w;
-          }
+        for (int e = 0; e < D; ++e) o[e] = 0.f;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int e = 0; e < D; e += 8) {
+          uint4 v;
+          v.x = pack2<T>(o[e] * inv, o[e + 1] * inv);
+          v.y = pack2<T>(o[e + 2] * inv, o[e + 3] * inv);
+          v.z = pack2<T>(o[e + 4] * inv, o[e + 5] * inv);
+          v.w = pack2<T>(o[e + 6] * inv, o[e + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + e) = v;
         }
       }
-      if (row_ok && p.lse != nullptr)
-        p.lse[static_cast<size_t>(qo_start + t0 + qi) * hq + h * G + gi] =
-            l > 0.f ? m_used + lg2(l) : -INFINITY;
+      if (row_ok && p.lse != nullptr) p.lse[row] = l > 0.f ? m_used + lg2(l) : -INFINITY;
+    }
+    tc_fence_before();
+    done_item(it);
+    kt += ntiles;
     }
   }
 
