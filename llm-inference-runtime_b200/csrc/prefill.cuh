@@ -728,7 +728,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const bool row_ok = r / G < QT && w.t0 + qi < w.qo_len;
       const size_t row = static_cast<size_t>(w.qo_start + w.t0 + qi) * hq + w.h * G + gi;
       T* orow = reinterpret_cast<T*>(p.out) + row * D;
-#pragma unroll
       // all of the row's O columns in one TMEM round trip (the scores'
       // registers are free here)
       float o[D];
