@@ -239,7 +239,8 @@ int encode_q_map(CUtensorMap* map, const void* q, int64_t stride_n, int64_t stri
 
 template <typename T, int D>
 int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
-                   const PrefillParams& prm, int64_t grid, int dev, cudaStream_t stream) {
+                   const CUtensorMap& om, const PrefillParams& prm, int64_t grid, int dev,
+                   cudaStream_t stream) {
   static std::atomic<uint64_t> done{0};
   constexpr int smem = PfCfg<D>::kSmemBytes;
   if (allow_smem(prefill_kernel<T, D>, smem, &done, dev) != cudaSuccess) return PA_ERR_CUDA;
@@ -247,7 +248,8 @@ int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorM
   // persistent: one CTA per SM at most, each taking items until none is left
   const int sms = sm_count(dev) > 0 ? sm_count(dev) : 148;
   grid = std::min<int64_t>(grid, sms);
-  prefill_kernel<T, D><<<static_cast<unsigned>(grid), kPfThreads, smem, stream>>>(qm, km, vm, prm);
+  prefill_kernel<T, D><<<static_cast<unsigned>(grid), kPfThreads, smem, stream>>>(qm, km, vm, om,
+                                                                                  prm);
   return launch_status();
 }
 
@@ -967,9 +969,13 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
   const int64_t max_items = prefill_max_items(batch_size, total_qo, hkv, 2 * qt);
   const PrefillWsLayout L = prefill_ws_layout(max_items);
   if (L.total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
-  CUtensorMap qm, km, vm;
+  CUtensorMap qm, km, vm, om;
   if ((st = encode_q_map(&qm, q, q_stride_n, q_stride_h, total_qo, num_qo_heads, D, G, qt,
                          cache->dtype)) != PA_OK)
+    return st;
+  // out [total_qo, num_qo_heads, head_dim]: the q map's shape and boxes
+  if ((st = encode_q_map(&om, out, static_cast<int64_t>(num_qo_heads) * D, D, total_qo,
+                         num_qo_heads, D, G, qt, cache->dtype)) != PA_OK)
     return st;
   if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage, 1)) != PA_OK) return st;
   if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage, 1)) != PA_OK) return st;
@@ -998,10 +1004,10 @@ int pa_prefill_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const 
   const int dev = current_device();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cache->dtype == PA_DTYPE_BF16)
-    return D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, p, max_items, dev, s)
-                   : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, p, max_items, dev, s);
-  return D == 64 ? launch_prefill<__half, 64>(qm, km, vm, p, max_items, dev, s)
-                 : launch_prefill<__half, 128>(qm, km, vm, p, max_items, dev, s);
+    return D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, om, p, max_items, dev, s)
+                   : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, om, p, max_items, dev, s);
+  return D == 64 ? launch_prefill<__half, 64>(qm, km, vm, om, p, max_items, dev, s)
+                 : launch_prefill<__half, 128>(qm, km, vm, om, p, max_items, dev, s);
 }
 
 }  // extern "C"
@@ -1122,9 +1128,14 @@ int cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int G = num_qo_heads / hkv;
   // ---- level 0: the shared prefix, key chunks as non-causal prefill requests
-  CUtensorMap qm, km, vm;
+  CUtensorMap qm, km, vm, om;
   if ((st = encode_q_map(&qm, q, q_stride_n, q_stride_h, batch_size, num_qo_heads, D, G, sh.qt,
                          cache->dtype)) != PA_OK)
+    return st;
+  // level-0 states: one [batch, num_qo_heads, head_dim] block per key chunk
+  if ((st = encode_q_map(&om, ws + L.o0, static_cast<int64_t>(num_qo_heads) * D, D,
+                         static_cast<int64_t>(sh.max_chunks) * batch_size, num_qo_heads, D, G,
+                         sh.qt, cache->dtype)) != PA_OK)
     return st;
   if ((st = encode_kv_map(&km, cache->k_base, *cache, kPage, 1)) != PA_OK) return st;
   if ((st = encode_kv_map(&vm, cache->v_base, *cache, kPage, 1)) != PA_OK) return st;
@@ -1152,10 +1163,12 @@ int cascade_run(const void* q, int64_t q_stride_n, int64_t q_stride_h, const pa_
                                        offsetof(PrefillPlanHeader, next_item));
   p.q_rows = reinterpret_cast<const int32_t*>(ws + L.q_rows);
   const bool bf16 = cache->dtype == PA_DTYPE_BF16;
-  st = bf16 ? (D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, p, L.prefill_items, dev, s)
-                       : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, p, L.prefill_items, dev, s))
-            : (D == 64 ? launch_prefill<__half, 64>(qm, km, vm, p, L.prefill_items, dev, s)
-                       : launch_prefill<__half, 128>(qm, km, vm, p, L.prefill_items, dev, s));
+  st = bf16 ? (D == 64 ? launch_prefill<__nv_bfloat16, 64>(qm, km, vm, om, p, L.prefill_items,
+                                                            dev, s)
+                       : launch_prefill<__nv_bfloat16, 128>(qm, km, vm, om, p, L.prefill_items,
+                                                             dev, s))
+            : (D == 64 ? launch_prefill<__half, 64>(qm, km, vm, om, p, L.prefill_items, dev, s)
+                       : launch_prefill<__half, 128>(qm, km, vm, om, p, L.prefill_items, dev, s));
   if (st != PA_OK) return st;
   // ---- level 1: each request's unique pages (positions of an appended token
   // are global; the plan recorded the prefix length they are taken from)

@@ -69,6 +69,7 @@ constexpr int kPfRelayVWarp = 11;  // V tiles
 constexpr int kPfBarP = 1;  // + t
 constexpr int kPfBarK = 3;
 constexpr int kPfBarV = 4;
+constexpr int kPfBarO = 5;  // warpgroup 1's output rows staged / staging buffer free
 constexpr int kPfBarPThreads = 128 + 32;
 constexpr int kPfBarKVThreads = 32 + 32;
 constexpr int kPfThreads = 384;
@@ -123,13 +124,20 @@ struct PfCfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  static constexpr int kOffBar = kOffV + kStages * kTileBytes;
+  // tile 1's output rows, staged for their TMA store (D / 64 panels of 128
+  // rows x 128 bytes, the layout of a Q tile; tile 0's go to Q tile 1's
+  // buffer)
+  static constexpr int kOffStage = kOffV + kStages * kTileBytes;
+  static constexpr int kStageBytes = kPfRows * D * 2;
+  static constexpr int kOffBar = kOffStage + kStageBytes;
   // barriers: q_full, s_full[2], o_done[2], mma_done, k_full/k_empty/v_full/v_empty[S],
-  // item_full[3], item_empty[3], q_empty
-  static constexpr int kNumBars = 6 + 4 * kStages + 7;
+  // item_full[3], item_empty[3], q_empty, q_full1, o0_staged
+  static constexpr int kNumBars = 6 + 4 * kStages + 9;
   static constexpr int kOffSlots = kOffBar + kNumBars * 8 + 16;  // three work-item slots
   static constexpr int kSmemBytes = kOffSlots + 3 * 64 + 1024;
   static_assert(kOffSlots % 8 == 0, "shared-memory alignment");
+  static_assert(kOffStage % 1024 == 0, "128-byte swizzled panels start on 1024 bytes");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
   // TMEM columns: S0 | S1 | O0 | O1 (P_t is written over the first half of S_t)
   static constexpr uint32_t kTmemCols = 512;
 };
@@ -293,7 +301,8 @@ __device__ __forceinline__ PfItem pf_item(const PrefillParams& p, int idx) {
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                   const __grid_constant__ CUtensorMap vmap, const PrefillParams p) {
+                   const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
+                   const PrefillParams p) {
   using C = PfCfg<D>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -301,8 +310,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint8_t* sQ = smem + C::kOffQ;
   uint8_t* sK = smem + C::kOffK;
   uint8_t* sV = smem + C::kOffV;
+  uint8_t* sO = smem + C::kOffStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-  uint64_t* q_full = bars + 0;
+  uint64_t* q_full = bars + 0;  // Q tile 0 landed
   uint64_t* s_full = bars + 1;  // [2] per Q tile
   uint64_t* o_done = bars + 3;    // [2]
   uint64_t* mma_done = bars + 5;  // every MMA of the CTA has completed
@@ -312,7 +322,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* v_empty = v_full + S;
   uint64_t* item_full = v_empty + S;   // [3] item slot published
   uint64_t* item_empty = item_full + 3;  // [3] every reader is done with it
-  uint64_t* q_empty = item_empty + 3;    // the item's S MMAs are done with the Q tiles
+  uint64_t* q_empty = item_empty + 3;    // the item's S_0 MMAs are done with Q tile 0
+  uint64_t* q_full1 = q_empty + 1;       // Q tile 1 landed
+  uint64_t* o0_staged = q_full1 + 1;     // tile 0 done with Q tile 1's buffer (rows staged there)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   PfItem* slots = reinterpret_cast<PfItem*>(smem + C::kOffSlots);
 
@@ -332,6 +344,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
+    prefetch_tensormap(&omap);
     mbar_init(q_full, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_full[t], 1);
@@ -349,6 +362,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     mbar_init(mma_done, 1);
     mbar_init(q_empty, 1);
+    mbar_init(q_full1, 1);
+    mbar_init(o0_staged, 4);
     fence_mbar_init();
   }
   if (warp == kPfMmaWarp) {
@@ -407,6 +422,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     publish(0, w);
     uint32_t kt = 0;  // K / V tiles loaded so far: ring position
     int qc = 0;       // items whose Q tiles were loaded
+    // Tile 0's output rows of item i - 1 wait in Q tile 1's buffer; once
+    // tile 0 has staged them, this warp stores them and lets the store read
+    // the buffer before item i's Q tile 1 lands in it.
+    bool prev_staged = false;
+    int prev_h = 0, prev_row = 0, nitems = 0;
+    auto release_q1 = [&](int i) {
+      if (!mbar_wait_warp(o0_staged, i & 1)) failed = true;
+      if (lane == 0 && prev_staged && !failed) {
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_store_3d(&omap, sQ + C::kQBytes + pn * C::kPanelBytes, pn * 64, prev_h * G,
+                       prev_row);
+        bulk_commit();
+        bulk_wait_read_all();
+      }
+      __syncwarp();
+    };
     for (int it = 0; w.ntiles >= 0; ++it) {
       // claim and publish item it + 1; its slot was item it - 2's
       const int nxt = claim();
@@ -414,59 +446,77 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         failed = true;
       const PfItem wn = pf_item(p, failed ? -1 : nxt);
       publish((it + 1) % 3, wn);
+      const int c1 = p.heads_inner ? w.h : 0, c2 = p.heads_inner ? 0 : w.h;
       if (w.ntiles > 0) {
-        const int c1 = p.heads_inner ? w.h : 0, c2 = p.heads_inner ? 0 : w.h;
-        // Q tiles, once the previous item's S MMAs are done with the buffer
+        // Q tile 0, once the previous item's S_0 MMAs are done with it
         if (qc > 0 && !mbar_wait_warp(q_empty, (qc - 1) & 1)) failed = true;
         ++qc;
         if (lane == 0) {
-          mbar_arrive_expect_tx(q_full, 2 * C::kQBytes);
+          mbar_arrive_expect_tx(q_full, C::kQBytes);
 #pragma unroll
-          for (int t = 0; t < 2; ++t)
-#pragma unroll
-            for (int pn = 0; pn < C::kPanels; ++pn)
-              tma_load_3d(sQ + t * C::kQBytes + pn * C::kPanelBytes, &qmap, q_full, pn * 64,
-                          w.h * G, w.q_row0 + w.t0 + t * QT);
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_3d(sQ + pn * C::kPanelBytes, &qmap, q_full, pn * 64, w.h * G,
+                        w.q_row0 + w.t0);
         }
-        for (int j = 0; j < w.ntiles; ++j) {
-          const uint32_t g = kt + j;
-          const int st = g % S, use = g / S;
-          const int np = min(8, w.npages - 8 * j);
-          int page = 0;
-          if (lane < np) {
-            page = __ldg(p.kv_indices + w.page0 + 8 * j + lane);
-            if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
-              set_status(PA_ERR_DEVICE_CHECK);
-              page = 0;
-            }
+      }
+      auto load_tile = [&](int j) {
+        const uint32_t g = kt + j;
+        const int st = g % S, use = g / S;
+        const int np = min(8, w.npages - 8 * j);
+        int page = 0;
+        if (lane < np) {
+          page = __ldg(p.kv_indices + w.page0 + 8 * j + lane);
+          if (static_cast<unsigned>(page) >= static_cast<unsigned long long>(p.num_pages)) {
+            set_status(PA_ERR_DEVICE_CHECK);
+            page = 0;
           }
-          const uint32_t bytes = static_cast<uint32_t>(np) * C::kPanels * 2048;
-          // after a timeout the stages still complete (no bytes expected), so
-          // the relays and the issuer keep their rounds without waiting long
-          if (use > 0 && !failed && !mbar_wait_warp(&k_empty[st], (use - 1) & 1)) failed = true;
-          if (lane == 0) mbar_arrive_expect_tx(&k_full[st], failed ? 0u : bytes);
-          __syncwarp();
-          if (lane < np && !failed) {
-#pragma unroll
-            for (int pn = 0; pn < C::kPanels; ++pn)
-              tma_load_4d(sK + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &kmap,
-                          &k_full[st], pn * 64, c1, c2, page);
-          }
-          if (use > 0 && !failed && !mbar_wait_warp(&v_empty[st], (use - 1) & 1)) failed = true;
-          if (lane == 0) mbar_arrive_expect_tx(&v_full[st], failed ? 0u : bytes);
-          __syncwarp();
-          if (lane < np && !failed) {
-#pragma unroll
-            for (int pn = 0; pn < C::kPanels; ++pn)
-              tma_load_4d(sV + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &vmap,
-                          &v_full[st], pn * 64, c1, c2, page);
-          }
-          __syncwarp();
         }
+        const uint32_t bytes = static_cast<uint32_t>(np) * C::kPanels * 2048;
+        // after a timeout the stages still complete (no bytes expected), so
+        // the relays and the issuer keep their rounds without waiting long
+        if (use > 0 && !failed && !mbar_wait_warp(&k_empty[st], (use - 1) & 1)) failed = true;
+        if (lane == 0) mbar_arrive_expect_tx(&k_full[st], failed ? 0u : bytes);
+        __syncwarp();
+        if (lane < np && !failed) {
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_4d(sK + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &kmap,
+                        &k_full[st], pn * 64, c1, c2, page);
+        }
+        if (use > 0 && !failed && !mbar_wait_warp(&v_empty[st], (use - 1) & 1)) failed = true;
+        if (lane == 0) mbar_arrive_expect_tx(&v_full[st], failed ? 0u : bytes);
+        __syncwarp();
+        if (lane < np && !failed) {
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_4d(sV + st * C::kTileBytes + pn * C::kPanelBytes + lane * 2048, &vmap,
+                        &v_full[st], pn * 64, c1, c2, page);
+        }
+        __syncwarp();
+      };
+      if (w.ntiles > 0) load_tile(0);
+      if (it > 0) release_q1(it - 1);
+      if (w.ntiles > 0) {
+        // Q tile 1, in the buffer the previous item's tile 0 output has left
+        if (lane == 0) {
+          mbar_arrive_expect_tx(q_full1, C::kQBytes);
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_3d(sQ + C::kQBytes + pn * C::kPanelBytes, &qmap, q_full1, pn * 64, w.h * G,
+                        w.q_row0 + w.t0 + QT);
+        }
+        for (int j = 1; j < w.ntiles; ++j) load_tile(j);
         kt += w.ntiles;
       }
+      // the rule tile 0's epilogue applies to this item
+      prev_staged = w.ntiles > 0 && w.t0 + QT <= w.qo_len;
+      prev_h = w.h;
+      prev_row = w.qo_start + w.t0;
+      nitems = it + 1;
       w = wn;
     }
+    if (nitems > 0) release_q1(nitems - 1);
+    if (lane == 0) bulk_wait_all();  // the stores have landed before the grid ends
     if (lane == 0) {
       if (failed) set_status(PA_ERR_TIMEOUT);
       // the last CTA to stop claiming resets the counter for the next launch
@@ -518,14 +568,21 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (w.ntiles < 0) break;
       if (w.ntiles == 0) continue;
       const int ntiles = w.ntiles;
+      // S_0 as soon as Q tile 0 and the first K tile are in; Q tile 1 lands
+      // after the previous item's tile 0 output has left its buffer
       if (!mbar_wait_warp(q_full, qc & 1)) failed = true;
-      ++qc;
       named_bar_sync(kPfBarK, kPfBarKVThreads);
       if (lane == 0) {
         tc_fence_after();
         issue_s(0, kt);
-        issue_s(1, kt);
         if (ntiles == 1) umma_commit(q_empty);
+      }
+      __syncwarp();
+      if (!mbar_wait_warp(q_full1, qc & 1)) failed = true;
+      ++qc;
+      if (lane == 0) {
+        tc_fence_after();
+        issue_s(1, kt);
       }
       __syncwarp();
       for (int j = 0; j < ntiles; ++j) {
@@ -557,7 +614,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // the next S_t overwrites P_t only after this PV (same thread, in order)
             if (j + 1 < ntiles) {
               issue_s(t, g + 1);
-              if (t == 1 && j + 2 == ntiles) umma_commit(q_empty);  // the item's last S
+              if (t == 0 && j + 2 == ntiles) umma_commit(q_empty);  // the item's last S_0
             }
           }
           __syncwarp();
@@ -719,43 +776,85 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (!failed && ntiles > 0) {
       if (!mbar_wait_warp(&o_done[t], (kt + ntiles - 1) & 1)) failed = true;
     }
+    // Output rows. Row r of a tile is query r / G, head r % G, and a row
+    // per thread makes every warp store touch 32 lines: D / 8 such stores
+    // per thread keep the SM's load / store path busy for microseconds at
+    // every item end, and the mbarrier polls of the issuer (the next item's
+    // Q) and of the softmax warps (its first scores) queue behind them. So
+    // both tiles' rows leave through TMA stores (one per 64-column panel:
+    // a tile is one 3-D box of the output, 64 dims x G heads x QT queries),
+    // staged in shared memory in the Q tile layout: tile 0's in Q tile 1's
+    // buffer (free once this item's S_1 MMAs are done; the producer stores
+    // them and then loads the next Q tile 1 there), tile 1's in a buffer of
+    // its own (its thread 0 stores them and checks at the next use that the
+    // store has read the buffer). A tile that runs past its request's rows
+    // (the rows after it belong to the next request) is written directly.
+    const PfItem& w = slots[it % 3];  // still this item's: released below
+    const bool staged = ntiles > 0 && w.t0 + (t + 1) * QT <= w.qo_len;
+    uint8_t* const stage = t == 0 ? sQ + C::kQBytes : sO;
+    if (t == 1 && staged) {
+      if (r == 0) bulk_wait_read_all();
+      named_bar_sync(kPfBarO, 128);
+    }
     if (failed) {
       set_status(PA_ERR_TIMEOUT);
     } else {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const PfItem& w = slots[it % 3];  // still this item's: released below
       const bool row_ok = r / G < QT && w.t0 + qi < w.qo_len;
       const size_t row = static_cast<size_t>(w.qo_start + w.t0 + qi) * hq + w.h * G + gi;
       T* orow = reinterpret_cast<T*>(p.out) + row * D;
-      // all of the row's O columns in one TMEM round trip (the scores'
-      // registers are free here)
-      float o[D];
-      if (ntiles > 0) {
+      const uint32_t srow = smem_u32(stage) + r * 128;
+      // 64 of the row's O columns per TMEM round trip (one panel)
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, o + c * 32);
-        tmem_wait_ld();
-      } else {
+      for (int pn = 0; pn < C::kPanels; ++pn) {
+        float o[64];
+        if (ntiles > 0) {
+          tmem_ld32(tO + pn * 64, o);
+          tmem_ld32(tO + pn * 64 + 32, o + 32);
+          tmem_wait_ld();
+        } else {
 #pragma unroll
-        for (int e = 0; e < D; ++e) o[e] = 0.f;
-      }
-      if (row_ok) {
+          for (int e = 0; e < 64; ++e) o[e] = 0.f;
+        }
 #pragma unroll
-        for (int e = 0; e < D; e += 8) {
+        for (int c = 0; c < 8; ++c) {
           uint4 v;
-          v.x = pack2<T>(o[e] * inv, o[e + 1] * inv);
-          v.y = pack2<T>(o[e + 2] * inv, o[e + 3] * inv);
-          v.z = pack2<T>(o[e + 4] * inv, o[e + 5] * inv);
-          v.w = pack2<T>(o[e + 6] * inv, o[e + 7] * inv);
-          *reinterpret_cast<uint4*>(orow + e) = v;
+          v.x = pack2<T>(o[8 * c] * inv, o[8 * c + 1] * inv);
+          v.y = pack2<T>(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+          v.z = pack2<T>(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+          v.w = pack2<T>(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          if (staged) {
+            // chunk c of row r at chunk c ^ (r % 8): the map's 128-byte swizzle
+            st_shared_u4(srow + pn * C::kPanelBytes + ((c ^ (r & 7)) * 16), v);
+          } else if (row_ok) {
+            *reinterpret_cast<uint4*>(orow + pn * 64 + 8 * c) = v;
+          }
         }
       }
+      if (staged) fence_proxy_async();
       if (row_ok && p.lse != nullptr) p.lse[row] = l > 0.f ? m_used + lg2(l) : -INFINITY;
+    }
+    if (t == 0) {
+      // every warp reports, staged or not, also after a timeout
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o0_staged);
+    } else if (staged) {
+      named_bar_sync(kPfBarO, 128);
+      if (r == 0 && !failed) {
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_store_3d(&omap, sO + pn * C::kPanelBytes, pn * 64, w.h * G,
+                       w.qo_start + w.t0 + QT);
+        bulk_commit();
+      }
     }
     tc_fence_before();
     done_item(it);
     kt += ntiles;
     }
+    // the output stores this thread issued have landed before the grid ends
+    if (t == 1 && r == 0) bulk_wait_all();
   }
 
   tc_fence_before();
