@@ -69,7 +69,7 @@ constexpr int kPfRelayVWarp = 11;  // V tiles
 constexpr int kPfBarP = 1;  // + t
 constexpr int kPfBarK = 3;
 constexpr int kPfBarV = 4;
-constexpr int kPfBarO = 5;  // warpgroup 1's output rows staged / staging buffer free
+constexpr int kPfBarO = 5;  // warpgroup 0's output rows staged / staging buffer free
 constexpr int kPfBarPThreads = 128 + 32;
 constexpr int kPfBarKVThreads = 32 + 32;
 constexpr int kPfThreads = 384;
@@ -124,17 +124,20 @@ struct PfCfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + 2 * kQBytes;
   static constexpr int kOffV = kOffK + kStages * kTileBytes;
-  // tile 1's output rows, staged for their TMA store (D / 64 panels of 128
-  // rows x 128 bytes, the layout of a Q tile; tile 0's go to Q tile 1's
-  // buffer)
+  // tile 0's output rows, staged for their TMA store (D / 64 panels of 128
+  // rows x 128 bytes, the layout of a Q or V tile; tile 1's go to the V
+  // stage of the item's last key tile)
   static constexpr int kOffStage = kOffV + kStages * kTileBytes;
   static constexpr int kStageBytes = kPfRows * D * 2;
   static constexpr int kOffBar = kOffStage + kStageBytes;
   // barriers: q_full, s_full[2], o_done[2], mma_done, k_full/k_empty/v_full/v_empty[S],
-  // item_full[3], item_empty[3], q_empty, q_full1, o0_staged
-  static constexpr int kNumBars = 6 + 4 * kStages + 9;
+  // item_full[3], item_empty[3], q_empty, q_full1, q_empty1, o1_staged[S]
+  static constexpr int kNumBars = 6 + 4 * kStages + 9 + kStages;
   static constexpr int kOffSlots = kOffBar + kNumBars * 8 + 16;  // three work-item slots
-  static constexpr int kSmemBytes = kOffSlots + 3 * 64 + 1024;
+  // per V stage: tile 1 rows to store (int4 entries, 16-byte aligned)
+  static constexpr int kOffPend = (kOffSlots + 3 * 64 + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kOffPend + kStages * 16 + 1024;
+  static_assert(kOffPend % 16 == 0, "int4 entries");
   static_assert(kOffSlots % 8 == 0, "shared-memory alignment");
   static_assert(kOffStage % 1024 == 0, "128-byte swizzled panels start on 1024 bytes");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
@@ -324,7 +327,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   uint64_t* item_empty = item_full + 3;  // [3] every reader is done with it
   uint64_t* q_empty = item_empty + 3;    // the item's S_0 MMAs are done with Q tile 0
   uint64_t* q_full1 = q_empty + 1;       // Q tile 1 landed
-  uint64_t* o0_staged = q_full1 + 1;     // tile 0 done with Q tile 1's buffer (rows staged there)
+  uint64_t* q_empty1 = q_full1 + 1;      // the item's S_1 MMAs are done with Q tile 1
+  uint64_t* o1_staged = q_empty1 + 1;    // [S] tile 1's rows are in V stage s
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
   PfItem* slots = reinterpret_cast<PfItem*>(smem + C::kOffSlots);
 
@@ -363,7 +367,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     mbar_init(mma_done, 1);
     mbar_init(q_empty, 1);
     mbar_init(q_full1, 1);
-    mbar_init(o0_staged, 4);
+    mbar_init(q_empty1, 1);
+    for (int s = 0; s < S; ++s) mbar_init(&o1_staged[s], 4);
     fence_mbar_init();
   }
   if (warp == kPfMmaWarp) {
@@ -422,20 +427,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     publish(0, w);
     uint32_t kt = 0;  // K / V tiles loaded so far: ring position
     int qc = 0;       // items whose Q tiles were loaded
-    // Tile 0's output rows of item i - 1 wait in Q tile 1's buffer; once
-    // tile 0 has staged them, this warp stores them and lets the store read
-    // the buffer before item i's Q tile 1 lands in it.
-    bool prev_staged = false;
-    int prev_h = 0, prev_row = 0, nitems = 0;
-    auto release_q1 = [&](int i) {
-      if (!mbar_wait_warp(o0_staged, i & 1)) failed = true;
-      if (lane == 0 && prev_staged && !failed) {
+    // Tile 1's output rows of an item wait in the V stage of the item's
+    // last key tile, which nothing reads again; before this warp loads the
+    // next V tile into that stage it stores the rows (once tile 1 has staged
+    // them) and lets the store read the stage. pend (shared memory, one
+    // entry per stage): staged or written directly, head, first row.
+    const uint32_t pend = smem_u32(smem + C::kOffPend);
+    uint32_t pend_mask = 0, pend_par = 0;  // stages with rows to store; o1_staged phases
+    auto flush_stage = [&](int st) {
+      if (!mbar_wait_warp(&o1_staged[st], (pend_par >> st) & 1)) failed = true;
+      pend_par ^= 1u << st;
+      pend_mask &= ~(1u << st);
+      if (lane == 0) {
+        const float4 e = ld_shared_f4(pend + st * 16);
+        if (__float_as_int(e.x) && !failed) {
 #pragma unroll
-        for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_store_3d(&omap, sQ + C::kQBytes + pn * C::kPanelBytes, pn * 64, prev_h * G,
-                       prev_row);
-        bulk_commit();
-        bulk_wait_read_all();
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_store_3d(&omap, sV + st * C::kTileBytes + pn * C::kPanelBytes, pn * 64,
+                         __float_as_int(e.y) * G, __float_as_int(e.z));
+          bulk_commit();
+          bulk_wait_read_all();
+        }
       }
       __syncwarp();
     };
@@ -484,6 +496,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         &k_full[st], pn * 64, c1, c2, page);
         }
         if (use > 0 && !failed && !mbar_wait_warp(&v_empty[st], (use - 1) & 1)) failed = true;
+        if ((pend_mask >> st) & 1) flush_stage(st);
         if (lane == 0) mbar_arrive_expect_tx(&v_full[st], failed ? 0u : bytes);
         __syncwarp();
         if (lane < np && !failed) {
@@ -494,10 +507,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         __syncwarp();
       };
-      if (w.ntiles > 0) load_tile(0);
-      if (it > 0) release_q1(it - 1);
       if (w.ntiles > 0) {
-        // Q tile 1, in the buffer the previous item's tile 0 output has left
+        load_tile(0);
+        // Q tile 1, once the previous item's S_1 MMAs are done with it
+        if (qc > 1 && !mbar_wait_warp(q_empty1, (qc - 2) & 1)) failed = true;
         if (lane == 0) {
           mbar_arrive_expect_tx(q_full1, C::kQBytes);
 #pragma unroll
@@ -507,15 +520,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         for (int j = 1; j < w.ntiles; ++j) load_tile(j);
         kt += w.ntiles;
+        // tile 1's rows will wait in the last tile's V stage (the rule the
+        // softmax warps apply)
+        const int st = (kt - 1) % S;
+        if (lane == 0)
+          st_shared_u4(pend + st * 16, make_uint4(w.t0 + 2 * QT <= w.qo_len ? 1u : 0u, w.h,
+                                                  w.qo_start + w.t0 + QT, 0u));
+        __syncwarp();
+        pend_mask |= 1u << st;
       }
-      // the rule tile 0's epilogue applies to this item
-      prev_staged = w.ntiles > 0 && w.t0 + QT <= w.qo_len;
-      prev_h = w.h;
-      prev_row = w.qo_start + w.t0;
-      nitems = it + 1;
       w = wn;
     }
-    if (nitems > 0) release_q1(nitems - 1);
+#pragma unroll 1
+    for (int k = 0; k < S; ++k)
+      if ((pend_mask >> ((kt + k) % S)) & 1) flush_stage((kt + k) % S);
     if (lane == 0) bulk_wait_all();  // the stores have landed before the grid ends
     if (lane == 0) {
       if (failed) set_status(PA_ERR_TIMEOUT);
@@ -568,8 +586,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (w.ntiles < 0) break;
       if (w.ntiles == 0) continue;
       const int ntiles = w.ntiles;
-      // S_0 as soon as Q tile 0 and the first K tile are in; Q tile 1 lands
-      // after the previous item's tile 0 output has left its buffer
+      // S_0 as soon as Q tile 0 and the first K tile are in, S_1 once Q tile
+      // 1 is in too
       if (!mbar_wait_warp(q_full, qc & 1)) failed = true;
       named_bar_sync(kPfBarK, kPfBarKVThreads);
       if (lane == 0) {
@@ -583,6 +601,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (lane == 0) {
         tc_fence_after();
         issue_s(1, kt);
+        if (ntiles == 1) umma_commit(q_empty1);
       }
       __syncwarp();
       for (int j = 0; j < ntiles; ++j) {
@@ -614,7 +633,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // the next S_t overwrites P_t only after this PV (same thread, in order)
             if (j + 1 < ntiles) {
               issue_s(t, g + 1);
-              if (t == 0 && j + 2 == ntiles) umma_commit(q_empty);  // the item's last S_0
+              if (j + 2 == ntiles) umma_commit(t == 0 ? q_empty : q_empty1);  // last S_t
             }
           }
           __syncwarp();
@@ -783,16 +802,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // Q) and of the softmax warps (its first scores) queue behind them. So
     // both tiles' rows leave through TMA stores (one per 64-column panel:
     // a tile is one 3-D box of the output, 64 dims x G heads x QT queries),
-    // staged in shared memory in the Q tile layout: tile 0's in Q tile 1's
-    // buffer (free once this item's S_1 MMAs are done; the producer stores
-    // them and then loads the next Q tile 1 there), tile 1's in a buffer of
-    // its own (its thread 0 stores them and checks at the next use that the
-    // store has read the buffer). A tile that runs past its request's rows
-    // (the rows after it belong to the next request) is written directly.
+    // staged in shared memory in the Q / V tile layout: tile 0's in a buffer
+    // of its own (its thread 0 stores them and checks at the next use that
+    // the store has read the buffer), tile 1's in the V stage of the item's
+    // last key tile, free once this item's PV_1 MMAs are done (the producer
+    // stores them before it loads the next V tile there). A tile that runs
+    // past its request's rows (the rows after it belong to the next
+    // request) is written directly.
     const PfItem& w = slots[it % 3];  // still this item's: released below
     const bool staged = ntiles > 0 && w.t0 + (t + 1) * QT <= w.qo_len;
-    uint8_t* const stage = t == 0 ? sQ + C::kQBytes : sO;
-    if (t == 1 && staged) {
+    const int vst = (kt + ntiles - 1) % S;  // V stage of the item's last tile
+    uint8_t* const stage = t == 0 ? sO : sV + vst * C::kTileBytes;
+    if (t == 0 && staged) {
       if (r == 0) bulk_wait_read_all();
       named_bar_sync(kPfBarO, 128);
     }
@@ -835,17 +856,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (staged) fence_proxy_async();
       if (row_ok && p.lse != nullptr) p.lse[row] = l > 0.f ? m_used + lg2(l) : -INFINITY;
     }
-    if (t == 0) {
-      // every warp reports, staged or not, also after a timeout
+    if (t == 1) {
+      // every warp reports, staged or not, also after a timeout (the
+      // producer holds the stage's next V load until then)
       __syncwarp();
-      if (lane == 0) mbar_arrive(o0_staged);
+      if (lane == 0 && ntiles > 0) mbar_arrive(&o1_staged[vst]);
     } else if (staged) {
       named_bar_sync(kPfBarO, 128);
       if (r == 0 && !failed) {
 #pragma unroll
         for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_store_3d(&omap, sO + pn * C::kPanelBytes, pn * 64, w.h * G,
-                       w.qo_start + w.t0 + QT);
+          tma_store_3d(&omap, sO + pn * C::kPanelBytes, pn * 64, w.h * G, w.qo_start + w.t0);
         bulk_commit();
       }
     }
@@ -854,7 +875,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     kt += ntiles;
     }
     // the output stores this thread issued have landed before the grid ends
-    if (t == 1 && r == 0) bulk_wait_all();
+    if (t == 0 && r == 0) bulk_wait_all();
   }
 
   tc_fence_before();
