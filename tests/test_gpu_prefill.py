@@ -126,6 +126,37 @@ def test_strided_q_from_fused_qkv(fi, workloads):
     _check(got, want)
 
 
+@pytest.mark.parametrize("geom_name", ["TINYLLAMA", "LLAMA3_8B"])
+def test_many_one_tile_items(fi, workloads, geom_name):
+    """Runs of items with a single key tile: the output rows of tile 1 wait
+    in the V ring stage of their item's last key tile until the next V load
+    into that stage, so several stages hold rows at once (the ring has 2
+    stages at head_dim 128, 4 at 64). Chunks of one or two item spans over
+    prefixes shorter than a key tile, some ending inside tile 1 (rows
+    written directly), then two launches on the same plan: identical
+    outputs, both equal to the oracle's."""
+    geom = getattr(workloads, geom_name)
+    span = 2 * (128 // (geom.num_qo_heads // geom.num_kv_heads))
+    g = torch.Generator().manual_seed(37)
+    n = 48
+    qo = [span * (1 + int(i % 3 == 0)) - (int(torch.randint(0, span // 2, (1,), generator=g))
+                                          if i % 4 == 1 else 0) for i in range(n)]
+    prefix = torch.randint(0, 128 - 2 * span + 1, (n,), generator=g).tolist()
+    prob = _problem(workloads, geom, qo, prefix, seed=38)
+    hq, d = prob.q.shape[1], prob.q.shape[2]
+    hkv = prob.pool.shape[3]
+    ws = torch.empty(128 << 20, dtype=torch.uint8, device=DEV)
+    w = fi.BatchPrefillWithPagedKVCacheWrapper(ws, "HND")
+    w.plan(_t(prob.qo_indptr), _t(prob.kv_indptr), _t(prob.kv_indices),
+           _t(prob.kv_last_page_len), hq, hkv, d, 16, q_data_type=prob.q.dtype)
+    q, pool = prob.q.to(DEV), prob.pool[0].to(DEV)
+    first = w.forward(q, pool, causal=True)
+    second = w.forward(q, pool, causal=True)
+    assert torch.equal(first, second)
+    want, _ = _oracle(prob)
+    _check(first.cpu(), want)
+
+
 def test_full_config3_sampled(fi, workloads):
     """Configuration 3 prefill part at full size: 16 chunks x 512 rows over
     prefixes U[0, 2048]; the oracle checks a sample of requests."""
