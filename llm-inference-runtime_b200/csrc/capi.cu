@@ -939,7 +939,8 @@ int pa_prefill_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
   if (!aligned16(workspace)) return PA_ERR_INVALID_ARGUMENT;
   const int64_t max_items = prefill_max_items(batch_size, total_qo, num_kv_heads, span);
   if (prefill_ws_layout(max_items).total > workspace_bytes) return PA_ERR_WORKSPACE_TOO_SMALL;
-  prefill_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+  // one thread per cost bucket (the plan's scan relies on it)
+  prefill_plan_kernel<<<1, kPfCostBuckets, 0, static_cast<cudaStream_t>(stream)>>>(
       qo_indptr, kv_indptr, kv_last_page_len, batch_size, total_qo, num_kv_indices, num_qo_heads,
       num_kv_heads, head_dim, page_size, span, max_items, static_cast<uint8_t*>(workspace));
   return launch_status();

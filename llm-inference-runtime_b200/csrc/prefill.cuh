@@ -27,7 +27,9 @@
 //     row (= TMEM lane): causal / length mask, online softmax in base 2 with
 //     lazy O rescaling (only when a row's max grows by more than 2^8), P back
 //     into TMEM, then a named barrier with the issuer; finally O is
-//     normalised and stored.
+//     normalised and staged in shared memory for TMA stores (tile 0 in a
+//     buffer of its own, tile 1 in the V stage of the item's last key tile,
+//     which the producer stores before reusing it).
 #pragma once
 
 #include "pa_common.cuh"
@@ -170,6 +172,7 @@ struct PrefillParams {
 // (counting sort on the number of K/V tiles a causal item visits), so the
 // hardware's in-order CTA dispatch approximates longest-processing-time.
 constexpr int kPfCostBuckets = 1024;
+static_assert(kPfCostBuckets == 1024, "the plan runs one thread per bucket, 32 warps");
 
 __global__ void prefill_plan_kernel(const int32_t* __restrict__ qo_indptr,
                                     const int32_t* __restrict__ kv_indptr,
@@ -223,16 +226,38 @@ __global__ void prefill_plan_kernel(const int32_t* __restrict__ qo_indptr,
       atomicOr(&s_err, 1);
   }
   __syncthreads();
-  // exclusive scan, most expensive bucket first (one thread; 1024 entries)
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int c = kPfCostBuckets - 1; c >= 0; --c) {
-      const int n = s_count[c];
-      s_count[c] = run;
-      run += n;
+  // exclusive scan, most expensive bucket first: thread i holds bucket
+  // kPfCostBuckets - 1 - i (the launch has one thread per bucket); a
+  // shuffle scan per warp, then one over the 32 warp totals
+  {
+    __shared__ int s_warp[32];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int c = kPfCostBuckets - 1 - static_cast<int>(threadIdx.x);
+    const int n = s_count[c];
+    int incl = n;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
     }
-    s_total = run;
-    if (run > max_items) s_err = 1;
+    if (lane == 31) s_warp[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      int w = s_warp[lane];
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, w, off);
+        if (lane >= off) w += v;
+      }
+      s_warp[lane] = w;  // inclusive prefix over warps 0 .. lane
+    }
+    __syncthreads();
+    const int before = (wid > 0 ? s_warp[wid - 1] : 0) + incl - n;
+    s_count[c] = before;
+    if (threadIdx.x == kPfCostBuckets - 1) {
+      s_total = before + n;
+      if (before + n > max_items) s_err = 1;
+    }
   }
   __syncthreads();
   const bool err = s_err != 0;
