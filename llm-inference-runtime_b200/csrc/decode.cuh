@@ -132,6 +132,13 @@ __device__ void decode_plan_block(const int32_t* __restrict__ kv_indptr,
   const int total = err ? 0 : static_cast<int>(total_ll);
   int q = (total + num_groups - 1) / num_groups;
   q = max(q, min_per_group);
+  // At most ~8 pieces per (request, head block) segment on average: the
+  // warp that merges a split segment reads its pieces two per L2 round
+  // trip, so short runs over long segments (32 requests of 256-2048 tokens
+  // over 444 groups: 6 pages per run, 12 pieces) cost more in merges than
+  // the extra groups gain.
+  const int segs = nhb * (batch - s_empty);
+  if (!err && segs > 0) q = max(q, (total + 8 * segs - 1) / (8 * segs));
   for (int w = threadIdx.x; w < num_groups; w += blockDim.x) {
     const long long s0 = static_cast<long long>(w) * q;
     int4 st = make_int4(0, 0, 0, 0);
