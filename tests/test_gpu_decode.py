@@ -192,6 +192,24 @@ def test_decode_plan_reuse_is_deterministic(fi, workloads):
     _check(outs[1], want)
 
 
+def test_mid_size_batch_capped_pieces(fi, workloads):
+    """32 TinyLlama requests of 256-2048 tokens: the plan's runs would be 6
+    pages (12 pieces per segment); they are raised so each segment splits
+    into about 8 pieces. Two launches on one plan agree bit for bit and
+    match the oracle."""
+    prob = workloads.make_decode_problem(workloads.TINYLLAMA, 32, 256, 2048, seed=13,
+                                         num_layers=1)
+    t = lambda a: torch.as_tensor(a).to(DEV)  # noqa: E731
+    w = fi.BatchDecodeWithPagedKVCacheWrapper(_ws(), "HND")
+    w.plan(t(prob.kv_indptr), t(prob.kv_indices), t(prob.kv_last_page_len), 32, 4, 64, 16)
+    q, pool = prob.q.to(DEV), prob.pool[0].to(DEV)
+    first, second = w.run(q, pool), w.run(q, pool)
+    assert torch.equal(first, second)
+    want, _ = attention.decode(prob.q, prob.pool[0].float(), prob.kv_indptr, prob.kv_indices,
+                               prob.kv_last_page_len)
+    _check(first, want)
+
+
 def test_config4_radix_shared_prefix_decode(fi, workloads):
     """Configuration 4: 64 requests share one 2048-token prefix (128 refcounted
     page ids from the radix cache) plus unique suffixes U[32, 256]; decode all,
